@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Decode throughput of the Llama-3-8B-shaped FP16 stack on B200 (libnpu_b200).
+
+Workload (N GPUs, tensor parallel): 32 decoder layers (hidden 4096, 32/8 heads of
+128, SwiGLU 14336, RMSNorm eps 1e-5, RoPE theta 5e5), final norm, LM head
+4096x128256 and greedy argmax; batch 64 sequences, each at position 4095 over a
+4095-token FP16 KV cache (4096 keys attended).  Weights are random-init FP16
+N(0, 0.02) and the cache N(0, 1), generated on the device (synthetic data of the
+config's shapes; nothing is downloaded).  One step reads ~49.4 GB, far more than
+the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N --steps K --warmup W]          # libnpu_b200
+    python bench.py --impl reference [--steps K --warmup W]  # CPU oracle arm
+
+Multi-GPU: launched by torchrun, one process per GPU; NCCL communicators come
+from torch.distributed (unique id broadcast) and the library's own all-reduces.
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s (Llama-3-8B shape, FP16) & % of HBM roofline"
+HIDDEN, HEADS, KV_HEADS, HEAD_DIM, FFN, VOCAB = 4096, 32, 8, 128, 14336, 128256
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--seq", type=int, default=4096, help="keys attended (position + 1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args(argv)
+    if a.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return a
+
+
+def step_bytes(batch, layers, seq, tp=1):
+    """Algorithmic HBM bytes of one decode step, whole job (FP16 weights and
+    every valid KV entry read once; the new K/V entries and outputs written once)."""
+    per_layer_w = (HEADS + 2 * KV_HEADS) * HEAD_DIM * HIDDEN + HIDDEN * HEADS * HEAD_DIM \
+        + 3 * FFN * HIDDEN + 2 * HIDDEN
+    kv = 2 * batch * KV_HEADS * (seq - 1) * HEAD_DIM
+    kv_new = 2 * batch * KV_HEADS * HEAD_DIM
+    acts = 2 * batch * HIDDEN  # layer input read / output written (FP16 equivalent)
+    top = VOCAB * HIDDEN + HIDDEN + batch * HIDDEN  # LM head, final norm, embedding rows
+    return 2 * (layers * (per_layer_w + kv + kv_new + acts) + top)
+
+
+def attention_bytes(batch, kv_heads, q_heads, seq):
+    """Algorithmic bytes of one flash-decoding launch: K and V of every attended
+    key, the queries read and the outputs written (FP16)."""
+    return 2 * (2 * batch * kv_heads * seq * HEAD_DIM + 2 * batch * q_heads * HEAD_DIM)
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per flash-decoding launch from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "flash_decode_b64_kv4096.md"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        if not self.uuid:
+            return
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.uuid}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx.append(float(r[1]))
+                for name, flag in zip(names, r[4:8]):
+                    if flag.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def cpu_baseline(batch, layers, seq, samples=3):
+    """The oracle (PyTorch on the host CPU, FP16 storage, FP32 compute) on a bounded
+    sample: one decoder layer and the LM head at the full batch and cache length,
+    extrapolated to the whole stack."""
+    import torch
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    shape = oracle.LLAMA3_8B
+    g = torch.Generator().manual_seed(5)
+
+    def h(*s, std=0.02):
+        return (torch.randn(*s, generator=g) * std).half()
+
+    w = {"self_attn.q_proj.weight": h(HEADS * HEAD_DIM, HIDDEN),
+         "self_attn.k_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
+         "self_attn.v_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
+         "self_attn.o_proj.weight": h(HIDDEN, HEADS * HEAD_DIM),
+         "mlp.gate_proj.weight": h(FFN, HIDDEN), "mlp.up_proj.weight": h(FFN, HIDDEN),
+         "mlp.down_proj.weight": h(HIDDEN, FFN),
+         "input_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16),
+         "post_attention_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16)}
+    k = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
+    v = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
+    lm = h(VOCAB, HIDDEN)
+    x = h(batch, HIDDEN, std=1.0)
+    pos = torch.full((batch,), seq - 1, dtype=torch.int32)
+    times = []
+    for _ in range(samples):
+        t0 = time.perf_counter()
+        y, _, _ = oracle.decoder_layer_decode(w, x, pos, k, v, shape, write_cache=False)
+        t1 = time.perf_counter()
+        logits = oracle.linear(oracle.rms_norm(y, torch.ones(HIDDEN), shape.eps), lm)
+        oracle.greedy_argmax(logits)
+        t2 = time.perf_counter()
+        times.append((t1 - t0) * layers + (t2 - t1))
+    t_step = statistics.median(times)
+    return {"value": batch / t_step, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle: 1 of {layers} layers + LM head at batch {batch}, {seq} keys, "
+                      f"x{layers} layers, median of {samples}",
+            "seconds_per_step": t_step}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    steps = []
+    base = None
+    for i in range(a.warmup + a.steps):
+        base = cpu_baseline(a.batch, a.layers, a.seq, samples=1)
+        if i >= a.warmup:
+            steps.append(base["seconds_per_step"])
+    t = statistics.median(steps)
+    value = a.batch / t
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s",
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic", "config": workload_config(a),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"],
+                             "kind": "port", "sample": base["sample"]},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(a):
+    return {"workload": f"llama3-8b-shaped {a.layers}-layer FP16 decode stack + LM head "
+                        f"4096x{VOCAB} + greedy argmax",
+            "global_batch": a.batch, "kv_len": a.seq, "position": a.seq - 1,
+            "layers": a.layers, "parallelism": f"tp{a.gpus}",
+            "l2": "inputs larger than L2 (~49 GB read per step), no flush"}
+
+
+def run_b200(a):
+    import torch
+    import torch.distributed as dist
+    from llm_compiler_3_b200 import _native, ops
+    from llm_compiler_3_b200.plan import llama3_8b
+    from llm_compiler_3_b200.runtime import Decoder, nccl_unique_id
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    nid = None
+    if world > 1:
+        box = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        nid = box[0]
+
+    plan = llama3_8b(layers=a.layers, max_batch=a.batch, max_seq=a.seq)
+    dec = Decoder(plan, device=local, tp_rank=rank, tp_size=world, nccl_id=nid)
+    info = dec.info
+    gen = torch.Generator(device=dev)
+
+    def randn(shape, seed, std):
+        gen.manual_seed(seed)
+        return (torch.randn(shape, device=dev, generator=gen) * std).half()
+
+    dec.set_weight("model.embed_tokens.weight", randn((VOCAB, HIDDEN), 11, 0.02))
+    dec.set_weight("lm_head.weight", randn((VOCAB, HIDDEN), 12, 0.02))
+    ones = torch.ones(HIDDEN, dtype=torch.float16, device=dev)
+    dec.set_weight("model.norm.weight", ones)
+    shapes = {"self_attn.q_proj.weight": (HEADS * HEAD_DIM, HIDDEN),
+              "self_attn.k_proj.weight": (KV_HEADS * HEAD_DIM, HIDDEN),
+              "self_attn.v_proj.weight": (KV_HEADS * HEAD_DIM, HIDDEN),
+              "self_attn.o_proj.weight": (HIDDEN, HEADS * HEAD_DIM),
+              "mlp.gate_proj.weight": (FFN, HIDDEN), "mlp.up_proj.weight": (FFN, HIDDEN),
+              "mlp.down_proj.weight": (HIDDEN, FFN)}
+    for layer in range(a.layers):
+        for j, (name, shape) in enumerate(shapes.items()):
+            dec.set_weight(f"model.layers.{layer}.{name}", randn(shape, 1000 + 16 * layer + j, 0.02))
+        dec.set_weight(f"model.layers.{layer}.input_layernorm.weight", ones)
+        dec.set_weight(f"model.layers.{layer}.post_attention_layernorm.weight", ones)
+        k, v = dec.kv_cache(layer)
+        gen.manual_seed(50000 + 2 * layer + 1000 * rank)
+        k[:, :, : a.seq - 1].normal_(generator=gen)
+        gen.manual_seed(50001 + 2 * layer + 1000 * rank)
+        v[:, :, : a.seq - 1].normal_(generator=gen)
+    torch.cuda.synchronize()
+
+    gen.manual_seed(7)
+    tokens = torch.randint(0, VOCAB, (a.batch,), device=dev, generator=gen, dtype=torch.int32)
+    positions = torch.full((a.batch,), a.seq - 1, dtype=torch.int32, device=dev)
+    ids = torch.empty(a.batch, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        dec.step_device(tokens, positions, ids)
+    torch.cuda.synchronize()
+    _native.device_status()
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        uuid = None
+    clocks = ClockSampler(uuid)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(a.steps):
+        dec.step_device(tokens, positions, ids)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop()
+    elapsed = max_over_ranks(start.elapsed_time(end) / 1e3)
+    status = _native.device_status()
+
+    # End to end through the public API with host buffers: H2D of tokens and
+    # positions, the step, D2H of the ids, every step.
+    tok_h = tokens.cpu().numpy()
+    pos_h = positions.cpu().numpy()
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        dec.step(tok_h, pos_h)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    e2e_elapsed = max_over_ranks(max(s2.elapsed_time(e2) / 1e3, wall))
+
+    # Dominant kernel (flash-decoding: ~70% of the step's bytes), timed alone on
+    # this rank's shard shape with CUDA events around graph replays that
+    # alternate between two layers' caches.
+    kv0 = dec.kv_cache(0)
+    kv1 = dec.kv_cache(1 if a.layers > 1 else 0)
+    q = torch.randn(a.batch, info["q_heads"], HEAD_DIM, device=dev).half()
+    out = torch.empty_like(q)
+    lens = torch.full((a.batch,), a.seq, dtype=torch.int32, device=dev)
+    ops.flash_decode(q, kv0[0], kv0[1], lens, out=out)
+    ops.flash_decode(q, kv1[0], kv1[1], lens, out=out)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    reps = 10
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            kv = kv0 if i % 2 == 0 else kv1
+            ops.flash_decode(q, kv[0], kv[1], lens, out=out)
+    graph.replay()
+    torch.cuda.synchronize()
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s3.record(stream)
+    graph.replay()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    fd_launch_s = s3.elapsed_time(e3) / 1e3 / reps
+    del graph
+
+    if rank != 0:
+        dec.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
+    peak, peak_kind = measured_peak()
+    fd_bytes = attention_bytes(a.batch, info["kv_heads"], info["q_heads"], a.seq)
+    fd_achieved = fd_bytes / fd_launch_s / 1e9
+    traffic = ncu_traffic()
+    if traffic is not None and world > 1:
+        traffic = traffic // world
+    t_step = elapsed / a.steps
+    value = a.batch * a.steps / elapsed
+    sb = step_bytes(a.batch, a.layers, a.seq)
+    per_step_launches = 1 + a.layers * (5 + (2 if world > 1 else 0)) + 2 + (1 if world > 1 else 0)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": t_step * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (random-init weights N(0,0.02), KV cache N(0,1), seeded on device)",
+        "config": workload_config(a),
+        "roofline": {"bound": "hbm", "kernel": "flash_decode", "achieved": fd_achieved,
+                     "peak": peak, "unit": "GB/s", "frac": fd_achieved / peak,
+                     "peak_source": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": fd_bytes,
+                     "launch_us": fd_launch_s * 1e6},
+        "step_roofline": {"algorithmic_bytes": sb, "achieved_GBps": sb / t_step / 1e9,
+                          "frac": sb / t_step / 1e9 / (peak * world), "peak_GBps": peak * world},
+        "e2e": {"value": a.batch * a.steps / e2e_elapsed, "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * 4 * a.batch, "d2h_bytes_per_step": 4 * a.batch},
+        "gpu_launches": per_step_launches * a.steps,
+        "device_error_bits": status,
+    }
+    if clock_info:
+        line["clocks"] = clock_info
+    if world == 1 and not a.no_cpu_baseline:
+        base = cpu_baseline(a.batch, a.layers, a.seq)
+        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+    dec.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    a = parse_args(argv)
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_b200(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

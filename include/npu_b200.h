@@ -1,0 +1,207 @@
+/*
+ * npu_b200.h -- C ABI of libnpu_b200, the B200 (sm_100a) execution backend for
+ * the FP16 Llama/Qwen3 decode computation that LLM_Compiler_3 lowers.
+ *
+ * Reference interface this replaces (all paths inside LLM_Compiler_3):
+ *   - the NPU back-end stages behind the pass registry: createTilePass,
+ *     createPlacePass, createHardwareOpsPass, createPipelineAttentionPass,
+ *     createAssignAddressesPass, createEmitPass, createEncodePass
+ *     (include/npu/Transforms/Passes.h:24-31) and their stage functions
+ *     (include/npu/Transforms/Pipeline.h:13-28);
+ *   - the package they produce (program.bin / system.json / hbm.bin,
+ *     tools/npu-compile/npu-compile.cpp:462-659) and the simulator that runs it
+ *     (test/Integration/harness.py:19-33).
+ * Instead of a package for a simulator, the B200 path hands a plan and the
+ * captured weights (arg<N>.bin, python/npu/capture/export.py:30-40) to this
+ * library, which runs them with hand-written sm_100a kernels.
+ *
+ * Conventions
+ *   - Every function returns int: NPU_B200_OK (0) or a negative NPU_B200_E_*.
+ *     On failure npu_b200_last_error() returns a thread-local message.  Nothing
+ *     throws across this boundary and no kernel traps.
+ *   - `stream` is a cudaStream_t passed as void*; 0 is the legacy default stream.
+ *     Kernel-level calls are stream-ordered and asynchronous.
+ *   - Pointers named d_* are device pointers; h_* are host pointers.
+ *   - A context is thread-compatible, not thread-safe.  Device buffers the
+ *     context allocates are owned by it; buffers passed in are borrowed.
+ *   - Tensors are dense, row-major, FP16 unless stated; shapes are in elements.
+ */
+#ifndef NPU_B200_H
+#define NPU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(NPU_B200_BUILD)
+#define NPU_B200_API __attribute__((visibility("default")))
+#else
+#define NPU_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NPU_B200_ABI_VERSION 1
+
+enum {
+  NPU_B200_OK = 0,
+  NPU_B200_E_INVALID = -1,     /* bad argument, shape or layout */
+  NPU_B200_E_CUDA = -2,        /* a CUDA runtime/driver call failed */
+  NPU_B200_E_NCCL = -3,        /* a NCCL call failed or NCCL could not be loaded */
+  NPU_B200_E_UNSUPPORTED = -4, /* valid request this build does not implement */
+  NPU_B200_E_NOMEM = -5,       /* device or host allocation failed */
+  NPU_B200_E_PLAN = -6,        /* plan file missing, malformed, or stamp mismatch */
+  NPU_B200_E_DEVICE = -7,      /* a kernel reported a device-side error (timeout, bounds) */
+  NPU_B200_E_STATE = -8        /* call out of order (e.g. decode before load) */
+};
+
+/* ---------------------------------------------------------------------------
+ * Library-wide
+ * ------------------------------------------------------------------------- */
+
+/* ABI version this library implements (NPU_B200_ABI_VERSION). */
+NPU_B200_API int npu_b200_abi_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+NPU_B200_API const char* npu_b200_last_error(void);
+
+/* Reads and clears the device error word on the current device.  *h_bits gets
+ * the OR of every device-side error since the last call (0 = none).
+ * Synchronizes the device.  Returns NPU_B200_E_DEVICE if any bit was set. */
+NPU_B200_API int npu_b200_device_status(uint32_t* h_bits);
+
+/* ---------------------------------------------------------------------------
+ * Kernel-level entry points (borrowed device buffers, stream-ordered)
+ * ------------------------------------------------------------------------- */
+
+/* Split-KV flash-decoding attention for one decode query per sequence.
+ *
+ * Replaces the NPU lowering of npu.attention (lib/Transforms/Attention.cpp:187-375,
+ * include/npu/Dialect/NPUDialect.td:147-189): per query head h with KV head
+ * h / group, out = softmax(scale * q K^T) V over keys [0, seq_lens[b]).
+ * Online softmax and every accumulator in FP32; output rounded once to FP16.
+ *
+ *   d_q        [batch, q_heads, head_dim]
+ *   d_k, d_v   [batch, kv_heads, max_seq, head_dim]   (KV cache, one layer)
+ *   d_seq_lens [batch] int32, each in [0, max_seq]; 0 keys gives a zero row
+ *   d_out      [batch, q_heads, head_dim]
+ *   head_dim in {64, 128}; group = q_heads / kv_heads in 1..8.
+ *   num_splits: key-range splits per (sequence, KV head); 0 chooses one.
+ *   d_workspace: npu_b200_flash_decode_workspace_size() bytes, zero-filled once
+ *     before first use; the kernel returns it to zero-filled state itself, so
+ *     calls on one stream may reuse it.  Calls that overlap on the GPU need
+ *     separate workspaces. */
+NPU_B200_API size_t npu_b200_flash_decode_workspace_size(int batch, int kv_heads, int head_dim, int max_seq,
+                                            int num_splits);
+NPU_B200_API int npu_b200_flash_decode(const void* d_q, const void* d_k, const void* d_v,
+                          const int32_t* d_seq_lens, void* d_out, int batch, int q_heads,
+                          int kv_heads, int head_dim, int max_seq, float scale, int num_splits,
+                          void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Linear layer on tcgen05 tensor cores:
+ *   out[b, n] = act( sum_k x[b, k] * w[n, k] + bias[n] ),  FP32 accumulation.
+ *
+ * Replaces the NPU matmul lowering (lib/Transforms/HardwareOps.cpp:105-155,
+ * lib/Transforms/Emit.cpp:348-378) of a legalized linalg.matmul with FP16
+ * operands and a zero accumulator (lib/Transforms/Legalize.cpp:136-161), plus the
+ * per-channel bias and the ReLU that normalizeGraph turns into maximumf
+ * (lib/Transforms/Normalize.cpp:494-507).
+ *
+ *   d_x    [batch, k] FP16, batch in 1..128 (the decode tokens)
+ *   d_w    [n_rows, k] FP16 (torch Linear layout, the capture's arg<N>.bin), k % 64 == 0
+ *   d_bias [n_rows] FP16 or NULL
+ *   d_out  [batch, n_rows] FP16, or FP32 with NPU_B200_LINEAR_OUT_F32
+ *   d_workspace: npu_b200_linear_workspace_size() bytes, 256-byte aligned,
+ *     zero-filled before first use and left zero-filled by every call. */
+#define NPU_B200_LINEAR_RELU 1
+#define NPU_B200_LINEAR_OUT_F32 2
+NPU_B200_API size_t npu_b200_linear_workspace_size(int n_rows, int k, int batch);
+NPU_B200_API int npu_b200_linear(const void* d_x, const void* d_w, const void* d_bias, void* d_out,
+                                 int batch, int n_rows, int k, int flags, void* d_workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode runtime (context-level).
+ *
+ * Replaces, for the B200 path, everything the reference runs after its front
+ * end: npu-tile / npu-place / npu-hw-ops / npu-pipeline-attention /
+ * npu-assign-addresses / npu-emit / encode-npu (include/npu/Transforms/Passes.h:24-31,
+ * run by tools/npu-compile/npu-compile.cpp:376-454), the hbm.bin image builder
+ * (npu-compile.cpp:495-659) and the simulator run (test/Integration/harness.py:19-33).
+ *
+ * A plan is a strict "key = value" text file (stage = cuda-plan, schema = 1,
+ * model shape, max_batch, max_seq), the counterpart of the reference's stamped
+ * stage files (npu-compile.cpp:226-316).  Weights are given by their transformers
+ * parameter names, whole (unsharded); each rank keeps its tensor-parallel shard.
+ * Each decode step runs as one CUDA graph per (entry point, batch), captured on
+ * first use; the first call for a batch size therefore must not happen inside
+ * another stream capture.
+ * ------------------------------------------------------------------------- */
+typedef struct npu_b200_ctx npu_b200_ctx;
+
+/* 128-byte NCCL unique id for tp_size > 1 (rank 0 makes it, every rank passes it
+ * to npu_b200_create).  NCCL is loaded on first use (NPU_B200_NCCL_LIBRARY
+ * overrides the library name). */
+NPU_B200_API int npu_b200_nccl_unique_id(void* h_out128);
+
+/* Context on `device` for rank tp_rank of tp_size (tensor parallel: q/k/v and
+ * gate/up column-sharded by heads / FFN columns, o/down row-sharded with one
+ * all-reduce each, LM head sharded by vocabulary).  nccl_unique_id may be NULL
+ * when tp_size == 1. */
+NPU_B200_API int npu_b200_create(int device, int tp_rank, int tp_size, const void* nccl_unique_id,
+                                 npu_b200_ctx** out);
+NPU_B200_API int npu_b200_destroy(npu_b200_ctx* ctx);
+
+/* Parse a plan and allocate this rank's weights, KV cache and buffers. */
+NPU_B200_API int npu_b200_load_plan(npu_b200_ctx* ctx, const char* plan_path);
+
+/* Parse and validate a plan without a GPU (the stage / schema / shape checks
+ * npu_b200_load_plan makes); out[] as npu_b200_plan_info with tp_size 1. */
+NPU_B200_API int npu_b200_plan_check(const char* plan_path, int64_t* out, int n);
+
+/* out[0..11] = layers, hidden, local q heads, local kv heads, local ffn, local vocab,
+ * vocab offset, max_batch, max_seq, head_dim, plan fingerprint (FNV-1a), tp_size. */
+NPU_B200_API int npu_b200_plan_info(const npu_b200_ctx* ctx, int64_t* out, int n);
+
+/* Copy one whole FP16 parameter (host or device memory) into this rank's layout.
+ * `name` is its transformers name, e.g. "model.layers.3.self_attn.q_proj.weight";
+ * a one-layer plan also accepts a captured block's names ("block.mlp.up_proj.weight"). */
+NPU_B200_API int npu_b200_set_weight(npu_b200_ctx* ctx, const char* name, const void* src,
+                                     size_t bytes);
+
+/* Read every weight of a capture directory written by CaptureResult.write
+ * (python/npu/capture/export.py:30-40: arguments.txt + arg<N>.bin). */
+NPU_B200_API int npu_b200_load_capture(npu_b200_ctx* ctx, const char* capture_dir);
+
+/* Device pointers of one layer's KV cache, each [max_batch][local kv heads][max_seq][head_dim]
+ * FP16; sequence b's key at position p lives at [b][h][p][:]. */
+NPU_B200_API int npu_b200_kv_cache(npu_b200_ctx* ctx, int layer, void** d_k, void** d_v);
+
+/* Greedy decode step of the whole stack: embed h_tokens[b], write K/V at
+ * h_positions[b] and attend positions [0, h_positions[b]] in every layer, final
+ * norm, LM head, argmax -> h_out_ids[b] (ties to the lowest id).  Host buffers;
+ * returns after the ids are copied back (synchronizes `stream`). */
+NPU_B200_API int npu_b200_decode_step(npu_b200_ctx* ctx, const int32_t* h_tokens,
+                                      const int32_t* h_positions, int batch, int32_t* h_out_ids,
+                                      void* stream);
+/* Same with device buffers; asynchronous on `stream`. */
+NPU_B200_API int npu_b200_decode_step_device(npu_b200_ctx* ctx, const int32_t* d_tokens,
+                                             const int32_t* d_positions, int batch,
+                                             int32_t* d_out_ids, void* stream);
+
+/* The layers only, on hidden states: x [batch, hidden] FP16 in, y [batch, hidden]
+ * FP16 out (the captured decoder layer's function, examples/llama/capture.py:38-54,
+ * as a decode step).  Host-buffer version synchronizes `stream`. */
+NPU_B200_API int npu_b200_forward_hidden(npu_b200_ctx* ctx, const void* h_x,
+                                         const int32_t* h_positions, int batch, void* h_y,
+                                         void* stream);
+NPU_B200_API int npu_b200_forward_hidden_device(npu_b200_ctx* ctx, const void* d_x,
+                                                const int32_t* d_positions, int batch, void* d_y,
+                                                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NPU_B200_H */

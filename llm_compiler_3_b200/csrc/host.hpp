@@ -1,0 +1,67 @@
+// Host-side helpers shared by the C-ABI translation units of libnpu_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/npu_b200.h"
+
+namespace npu_b200 {
+
+// Thread-local error message behind npu_b200_last_error().
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+
+// Returns NPU_B200_E_CUDA with a message if `e` is an error.
+int check_cuda(cudaError_t e, const char* what);
+
+#define NPU_TRY_CUDA(expr)                                   \
+  do {                                                       \
+    int _rc = ::npu_b200::check_cuda((expr), #expr);         \
+    if (_rc != NPU_B200_OK) return _rc;                      \
+  } while (0)
+
+#define NPU_REQUIRE(cond, ...)                                       \
+  do {                                                               \
+    if (!(cond)) return ::npu_b200::set_error(NPU_B200_E_INVALID, __VA_ARGS__); \
+  } while (0)
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// 2-D tensor map over a row-major FP16 matrix [rows, cols] with a box of
+// box_cols x box_rows elements and the 128-byte swizzle.  box_cols * 2 must be
+// <= 128.  The base must be 16-byte aligned and cols * 2 a multiple of 16.
+int make_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                       uint32_t box_rows, uint32_t box_cols);
+
+// Launch helper: enables programmatic dependent launch when `pdl` is set.
+struct LaunchCfg {
+  dim3 grid, block;
+  size_t smem = 0;
+  cudaStream_t stream = nullptr;
+  bool pdl = false;
+};
+
+template <typename... KArgs, typename... Args>
+int launch(const LaunchCfg& c, void (*kernel)(KArgs...), Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = c.grid;
+  cfg.blockDim = c.block;
+  cfg.dynamicSmemBytes = c.smem;
+  cfg.stream = c.stream;
+  cudaLaunchAttribute attr[1];
+  if (c.pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...),
+                    "cudaLaunchKernelEx");
+}
+
+}  // namespace npu_b200

@@ -1,0 +1,572 @@
+// Decode projections on 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Replaces the NPU matmul lowering (lib/Transforms/HardwareOps.cpp:105-155
+// convertMatmul, lib/Transforms/Emit.cpp:348-378 matrix write-out): FP16
+// operands, FP32 accumulation from zero, one rounding at the store
+// (lib/Transforms/Normalize.cpp:123-192 foldAccumulateAndRound).
+//
+// Shape of the problem at decode: W [N, K] is large and read once, X [B, K]
+// (B = tokens) is tiny.  So the weight is the M=128 operand ("swap AB"), the
+// tokens are the N=BN columns (16..128), and the accumulator tile 128 x BN
+// lives in tensor memory.  Weights stream through an S-stage TMA ring
+// (128-byte swizzle, L2 evict-first); the k-loop is split "stream-K" over
+// exactly one CTA per SM, so every SM pulls the same number of weight bytes
+// whatever N and K are.  A tile whose k-range spans several CTAs is finished by
+// the last of them to arrive, which adds the others' FP32 partials in CTA
+// order (deterministic) before the fused epilogue runs.
+//
+// Warp roles (192 threads): warps 0-3 epilogue (TMEM lanes 0-127 = tile rows),
+// warp 4 TMA producer, warp 5 MMA issuer.  Two TMEM accumulators let the MMA of
+// the next tile overlap the epilogue of the previous one.
+#include <math.h>
+
+#include "common.cuh"
+#include "host.hpp"
+#include "proj.cuh"
+
+namespace npu_b200 {
+namespace {
+
+constexpr int kEpiThreads = 128;
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 12;
+constexpr int kSmemBudget = 232448;  // 227 KB opt-in limit per block
+
+template <int BN>
+struct ProjShape {
+  static constexpr int kABytes = 128 * 64 * 2;  // one 128-row x 64-k weight block
+  static constexpr int kBBytes = BN * 64 * 2;   // one BN-token x 64-k activation block
+  static constexpr int kStageBytes = (kABytes + kBBytes + 1023) / 1024 * 1024;
+  static constexpr int kPitch = 128 + 4;        // floats per token column of the epilogue tile
+  static constexpr int kTileBytes = kPitch * BN * 4;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kMiscBytes = 512 + 8 * BN;  // barriers, TMEM slot, per-token scalars
+};
+
+__device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
+}
+
+// Barrier over the epilogue warps that also ORs a predicate across them, so all
+// 128 threads take the same branch afterwards.
+__device__ __forceinline__ bool epi_sync_or(bool pred) {
+  uint32_t any;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(any)
+      : "r"(static_cast<uint32_t>(pred)), "r"(kEpiThreads)
+      : "memory");
+  return any != 0;
+}
+
+// CTA whose stream-K range contains iteration i.
+__device__ __forceinline__ int owner_cta(long long i, long long total, int grid) {
+  long long c = (i * grid) / total;
+  while (c + 1 < grid && ((c + 1) * total) / grid <= i) ++c;
+  while (c > 0 && (c * total) / grid > i) --c;
+  return static_cast<int>(c);
+}
+
+template <int BN>
+__device__ __forceinline__ void run_epilogue(const EpiParams& ep, int tile, int r, float (&v)[BN],
+                                             const float* rn, float* tile_s, float* aux) {
+  using S = ProjShape<BN>;
+  constexpr int P = S::kPitch;
+  const int batch = ep.batch;
+#pragma unroll
+  for (int b = 0; b < BN; ++b) v[b] *= rn[b];
+
+  if (ep.kind == kEpiStore) {
+    const int n = tile * 128 + r;
+    if (n < ep.n_rows) {
+      const float bias = ep.bias ? __half2float(ep.bias[n]) : 0.f;
+#pragma unroll
+      for (int b = 0; b < BN; ++b) {
+        if (b < batch) {
+          float val = v[b] + bias;
+          if (ep.relu) val = fmaxf(val, 0.f);
+          const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
+          if (ep.out_f32)
+            static_cast<float*>(ep.out)[off] = val;
+          else
+            static_cast<__half*>(ep.out)[off] = __float2half_rn(val);
+        }
+      }
+    }
+  } else if (ep.kind == kEpiResid) {
+    const int n = tile * 128 + r;
+    const bool valid = n < ep.n_rows;
+    const float w = valid ? __half2float(ep.norm_w[n]) : 0.f;
+#pragma unroll
+    for (int b = 0; b < BN; ++b) {
+      float h2 = 0.f;
+      if (valid && b < batch) {
+        float* rp = ep.resid + static_cast<size_t>(b) * ep.ld_resid + n;
+        const float h = *rp + v[b];
+        *rp = h;
+        ep.xw[static_cast<size_t>(b) * ep.ld_xw + n] = __float2half_rn(h * w);
+        h2 = h * h;
+      }
+      tile_s[b * P + r] = h2;
+    }
+    epi_sync();
+    if (r < batch) {
+      float s = 0.f;
+      for (int i = 0; i < 128; ++i) s += tile_s[r * P + i];
+      ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + r] = s;
+    }
+    epi_sync();
+  } else if (ep.kind == kEpiSwiGLU) {
+#pragma unroll
+    for (int b = 0; b < BN; ++b) tile_s[b * P + r] = v[b];
+    epi_sync();
+    const int j = tile * 64 + r;
+    if (r < 64 && j < ep.n_rows / 2) {
+      for (int b = 0; b < batch; ++b) {
+        const float g = tile_s[b * P + r];
+        const float u = tile_s[b * P + r + 64];
+        const float act = g / (1.f + expf(-g)) * u;
+        static_cast<__half*>(ep.out)[static_cast<size_t>(b) * ep.ld_out + j] = __float2half_rn(act);
+      }
+    }
+    epi_sync();
+  } else if (ep.kind == kEpiQKV) {
+    const bool is_q = tile < ep.q_heads;
+    const bool is_k = !is_q && tile < ep.q_heads + ep.kv_heads;
+    const __half* nw = is_q ? ep.q_norm_w : (is_k ? ep.k_norm_w : nullptr);
+    if (nw) {  // per-head RMSNorm over the 128 dims (Qwen3 q_norm / k_norm)
+#pragma unroll
+      for (int b = 0; b < BN; ++b) tile_s[b * P + r] = v[b] * v[b];
+      epi_sync();
+      if (r < BN) {
+        float s = 0.f;
+        for (int i = 0; i < 128; ++i) s += tile_s[r * P + i];
+        aux[r] = rsqrtf(s * (1.f / 128.f) + ep.qk_eps);
+      }
+      epi_sync();
+      const float wr = __half2float(nw[r]);
+#pragma unroll
+      for (int b = 0; b < BN; ++b) v[b] = v[b] * aux[b] * wr;
+    }
+    if (is_q || is_k) {  // RoPE: rotate_half pairs (i, i + 64)
+#pragma unroll
+      for (int b = 0; b < BN; ++b) tile_s[b * P + r] = v[b];
+      epi_sync();
+      const float f = ep.inv_freq[r & 63];
+#pragma unroll
+      for (int b = 0; b < BN; ++b) {
+        if (b < batch) {
+          const float partner = tile_s[b * P + (r ^ 64)];
+          const float theta = static_cast<float>(ep.positions[b]) * f;
+          float sn, cs;
+          sincosf(theta, &sn, &cs);
+          v[b] = r < 64 ? v[b] * cs - partner * sn : v[b] * cs + partner * sn;
+        }
+      }
+      epi_sync();
+    }
+    if (is_q) {
+      __half* q = static_cast<__half*>(ep.out);
+#pragma unroll
+      for (int b = 0; b < BN; ++b)
+        if (b < batch)
+          q[static_cast<size_t>(b) * ep.ld_out + tile * 128 + r] = __float2half_rn(v[b]);
+    } else {
+      const int kh = is_k ? tile - ep.q_heads : tile - ep.q_heads - ep.kv_heads;
+      __half* cache = is_k ? ep.k_cache : ep.v_cache;
+#pragma unroll
+      for (int b = 0; b < BN; ++b) {
+        if (b < batch) {
+          const int pos = ep.positions[b];
+          if (pos < 0 || pos >= ep.max_seq) {
+            if (r == 0) report_error(kDevErrBounds);
+          } else {
+            cache[static_cast<size_t>(b) * ep.cache_batch_stride +
+                  (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + r] = __float2half_rn(v[b]);
+          }
+        }
+      }
+    }
+  } else if (ep.kind == kEpiArgmax) {
+    const int n = tile * 128 + r;
+    const bool valid = n < ep.n_rows;
+#pragma unroll
+    for (int b = 0; b < BN; ++b) tile_s[b * P + r] = valid ? v[b] : -INFINITY;
+    epi_sync();
+    if (r < batch) {
+      float best = -INFINITY;
+      int bi = tile * 128;
+      for (int i = 0; i < 128; ++i) {
+        const float x = tile_s[r * P + i];
+        if (x > best) {
+          best = x;
+          bi = tile * 128 + i;
+        }
+      }
+      ep.am_val[static_cast<size_t>(tile) * ep.am_ld + r] = best;
+      ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + r] = bi;
+    }
+    epi_sync();
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                const __grid_constant__ EpiParams ep, int n_tiles, int kblocks, int stages,
+                float* __restrict__ slots, uint32_t* __restrict__ counters) {
+  using S = ProjShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  float* tile_s = reinterpret_cast<float*>(smem + stages * S::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tile_s) + S::kTileBytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* rn = reinterpret_cast<float*>(tmem_slot + 4);  // [BN] input RMSNorm scale per token
+  float* aux = rn + BN;                                  // [BN] per-token scratch
+  volatile int* flags = reinterpret_cast<volatile int*>(aux + BN);  // [0] abort, [1] last
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long total = static_cast<long long>(n_tiles) * kblocks;
+  const int grid = gridDim.x, cta = blockIdx.x;
+  const long long it_begin = static_cast<long long>(cta) * total / grid;
+  const long long it_end = static_cast<long long>(cta + 1) * total / grid;
+
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(&wmap);
+    prefetch_tensormap(&xmap);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpiThreads);
+    }
+    mbar_init(drain, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const int n_iter = static_cast<int>(it_end - it_begin);
+      const int pre = min(stages, n_iter);
+      // Weights do not depend on the previous kernel: start streaming them
+      // before waiting for it; the activations follow once it has finished.
+      for (int i = 0; i < pre; ++i) {
+        const long long it = it_begin + i;
+        const int tile = static_cast<int>(it / kblocks), kb = static_cast<int>(it % kblocks);
+        uint8_t* st = smem + i * S::kStageBytes;
+        mbar_arrive_expect_tx(&full[i], S::kABytes + S::kBBytes);
+        tma_load_2d_hint(st, &wmap, &full[i], kb * 64, tile * 128, pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const int kb = static_cast<int>((it_begin + i) % kblocks);
+        tma_load_2d(smem + i * S::kStageBytes + S::kABytes, &xmap, &full[i], kb * 64, 0);
+      }
+      int issued = pre;
+      for (int i = pre; i < n_iter; ++i) {
+        const int s = i % stages;
+        if (flags[0] || !mbar_wait(&empty[s], ((i / stages) - 1) & 1, kDevErrMmaTimeout)) {
+          flags[0] = 1;
+          break;
+        }
+        const long long it = it_begin + i;
+        const int tile = static_cast<int>(it / kblocks), kb = static_cast<int>(it % kblocks);
+        uint8_t* st = smem + s * S::kStageBytes;
+        mbar_arrive_expect_tx(&full[s], S::kABytes + S::kBBytes);
+        tma_load_2d_hint(st, &wmap, &full[s], kb * 64, tile * 128, pol_w);
+        tma_load_2d(st + S::kABytes, &xmap, &full[s], kb * 64, 0);
+        issued = i + 1;
+      }
+      if (flags[0]) {  // leave no copy in flight into this CTA's shared memory
+        for (int i = max(0, issued - stages); i < issued; ++i)
+          mbar_wait(&full[i % stages], (i / stages) & 1, kDevErrTmaTimeout);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      long long it = it_begin;
+      int i = 0, seg = 0;
+      while (it < it_end && !flags[0]) {
+        const int tile = static_cast<int>(it / kblocks);
+        const long long seg_end = min(it_end, static_cast<long long>(tile + 1) * kblocks);
+        const int acc = seg & 1, use = seg >> 1;
+        if (seg >= 2 && !mbar_wait(&tempty[acc], (use - 1) & 1, kDevErrEpilogueTimeout)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool first = true;
+        for (; it < seg_end; ++it, ++i) {
+          const int s = i % stages;
+          if (flags[0] || !mbar_wait(&full[s], (i / stages) & 1, kDevErrTmaTimeout)) {
+            flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * S::kStageBytes);
+          const uint32_t b = a + S::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(d_tmem, smem_desc_sw128(a + kk * 32), smem_desc_sw128(b + kk * 32), idesc,
+                       (first && kk == 0) ? 0u : 1u);
+          first = false;
+          tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (flags[0]) break;
+        tc_commit(&tfull[acc]);
+        ++seg;
+      }
+      if (flags[0]) {  // no MMA may still write TMEM when it is released
+        tc_commit(drain);
+        mbar_wait(drain, 0, kDevErrMmaTimeout);
+      }
+    }
+  } else {
+    // ---------------- epilogue (tile row r = TMEM lane r) ----------------
+    const int r = threadIdx.x;
+    pdl_wait();
+    if (r < BN) {
+      float scale = 1.f;
+      if (ep.ssq_in != nullptr && r < ep.batch) {
+        float s = 0.f;
+        for (int p = 0; p < ep.ssq_parts; ++p) s += ep.ssq_in[static_cast<size_t>(p) * ep.ssq_ld + r];
+        scale = rsqrtf(s * ep.ssq_inv_hidden + ep.ssq_eps);
+      }
+      rn[r] = scale;
+    }
+    epi_sync();
+    long long it = it_begin;
+    int seg = 0;
+    while (it < it_end) {
+      const int tile = static_cast<int>(it / kblocks);
+      const int kb0 = static_cast<int>(it % kblocks);
+      const long long seg_end = min(it_end, static_cast<long long>(tile + 1) * kblocks);
+      const int acc = seg & 1, use = seg >> 1;
+      const bool bad = flags[0] || !mbar_wait(&tfull[acc], use & 1, kDevErrMmaTimeout);
+      if (epi_sync_or(bad)) {
+        flags[0] = 1;
+        break;
+      }
+      tc_fence_after();
+      float v[BN];
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + acc * BN;
+#pragma unroll
+      for (int j = 0; j < BN / 16; ++j) {
+        uint32_t rr[16];
+        tmem_ld16(taddr + j * 16, rr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v[j * 16 + q] = __uint_as_float(rr[q]);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+
+      const bool whole = kb0 == 0 && seg_end == static_cast<long long>(tile + 1) * kblocks;
+      bool mine = true;
+      if (!whole) {
+        // Stream-K fix-up: publish this CTA's partial; the last contributor
+        // adds all of them in CTA order.  Slot index tile + cta is unique.
+        float* slot = slots + static_cast<size_t>(tile + cta) * 128 * BN;
+#pragma unroll
+        for (int b = 0; b < BN; ++b) __stcg(slot + b * 128 + r, v[b]);
+        __threadfence();
+        epi_sync();
+        const int cf = owner_cta(static_cast<long long>(tile) * kblocks, total, grid);
+        const int cl = owner_cta(static_cast<long long>(tile + 1) * kblocks - 1, total, grid);
+        if (r == 0) {
+          const uint32_t prev = atomicAdd(&counters[tile], 1u);
+          flags[1] = (prev == static_cast<uint32_t>(cl - cf)) ? 1 : 0;
+        }
+        epi_sync();
+        mine = flags[1] != 0;
+        if (mine) {
+          __threadfence();
+          float sum[BN];
+#pragma unroll
+          for (int b = 0; b < BN; ++b) sum[b] = 0.f;
+          for (int c = cf; c <= cl; ++c) {
+            if (c == cta) {
+#pragma unroll
+              for (int b = 0; b < BN; ++b) sum[b] += v[b];
+            } else {
+              const float* other = slots + static_cast<size_t>(tile + c) * 128 * BN;
+#pragma unroll
+              for (int b = 0; b < BN; ++b) sum[b] += __ldcg(other + b * 128 + r);
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < BN; ++b) v[b] = sum[b];
+          if (r == 0) counters[tile] = 0u;  // leave the workspace reusable
+        }
+      }
+      if (mine) run_epilogue<BN>(ep, tile, r, v, rn, tile_s, aux);
+      it = seg_end;
+      ++seg;
+    }
+  }
+
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+template <int BN>
+int stages_for() {
+  using S = ProjShape<BN>;
+  const int fixed = 1024 + S::kTileBytes + S::kMiscBytes;
+  int st = (kSmemBudget - fixed) / S::kStageBytes;
+  return st > kMaxStages ? kMaxStages : st;
+}
+
+template <int BN>
+size_t smem_for(int stages) {
+  using S = ProjShape<BN>;
+  return 1024 + static_cast<size_t>(stages) * S::kStageBytes + S::kTileBytes + S::kMiscBytes;
+}
+
+int bn_for(int batch) { return batch <= 16 ? 16 : batch <= 32 ? 32 : batch <= 64 ? 64 : 128; }
+
+struct Geometry {
+  int bn, n_tiles, kblocks, grid;
+  size_t counter_bytes, slot_bytes;
+};
+
+Geometry geometry(int n_rows, int k, int batch) {
+  Geometry g;
+  g.bn = bn_for(batch);
+  g.n_tiles = (n_rows + 127) / 128;
+  g.kblocks = k / 64;
+  const long long total = static_cast<long long>(g.n_tiles) * g.kblocks;
+  g.grid = static_cast<int>(total < sm_count() ? total : sm_count());
+  g.counter_bytes = (static_cast<size_t>(g.n_tiles) * 4 + 255) / 256 * 256;
+  g.slot_bytes = static_cast<size_t>(g.n_tiles + g.grid - 1) * 128 * g.bn * 4;
+  return g;
+}
+
+template <int BN>
+int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& ep,
+                const Geometry& g, float* slots, uint32_t* counters, cudaStream_t stream,
+                bool pdl) {
+  const int stages = stages_for<BN>();
+  const size_t smem = smem_for<BN>(stages);
+  auto kern = proj_kernel<BN>;
+  NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  LaunchCfg cfg;
+  cfg.grid = dim3(g.grid);
+  cfg.block = dim3(kThreads);
+  cfg.smem = smem;
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, kern, wm, xm, ep, g.n_tiles, g.kblocks, stages, slots, counters);
+}
+
+}  // namespace
+
+size_t proj_workspace_bytes(int n_rows, int k, int batch) {
+  if (n_rows < 1 || k < 64 || batch < 1) return 0;
+  const Geometry g = geometry(n_rows, k, batch);
+  return g.counter_bytes + g.slot_bytes;
+}
+
+int proj_run(const void* w, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
+             void* workspace, size_t workspace_bytes, cudaStream_t stream, bool pdl) {
+  NPU_REQUIRE(w && x, "projection: null weight or activation pointer");
+  NPU_REQUIRE(n_rows >= 1 && k >= 64 && k % 64 == 0,
+              "projection: need rows >= 1 and K a positive multiple of 64 (rows=%d K=%d)", n_rows,
+              k);
+  NPU_REQUIRE(batch >= 1 && batch <= 128, "projection: batch %d not in [1, 128]", batch);
+  NPU_REQUIRE(ep.batch == batch && ep.n_rows == n_rows, "projection: epilogue shape mismatch");
+  NPU_REQUIRE((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+              "projection: W and X must be 16-byte aligned");
+  if (ep.kind == kEpiQKV)
+    NPU_REQUIRE(n_rows == (ep.q_heads + 2 * ep.kv_heads) * 128 && ep.positions && ep.inv_freq &&
+                    ep.k_cache && ep.v_cache && ep.out && ep.max_seq > 0,
+                "projection: QKV epilogue needs 128-dim heads, positions, RoPE table and caches");
+  if (ep.kind == kEpiSwiGLU)
+    NPU_REQUIRE(n_rows % 128 == 0 && ep.out, "projection: SwiGLU rows must be [gate64|up64] blocks");
+  if (ep.kind == kEpiResid)
+    NPU_REQUIRE(ep.resid && ep.norm_w && ep.xw && ep.ssq_out,
+                "projection: residual epilogue needs resid, norm weight, xw and ssq outputs");
+  if (ep.kind == kEpiArgmax) NPU_REQUIRE(ep.am_val && ep.am_idx, "projection: argmax outputs");
+  if (ep.kind == kEpiStore) NPU_REQUIRE(ep.out != nullptr, "projection: null output");
+
+  const Geometry g = geometry(n_rows, k, batch);
+  const size_t need = g.counter_bytes + g.slot_bytes;
+  NPU_REQUIRE(workspace && workspace_bytes >= need,
+              "projection: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  NPU_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+              "projection: workspace must be 256-byte aligned");
+  CUtensorMap wm, xm;
+  int rc = make_tensor_map_2d(&wm, w, n_rows, k, 128, 64);
+  if (rc) return rc;
+  rc = make_tensor_map_2d(&xm, x, batch, k, g.bn, 64);
+  if (rc) return rc;
+  uint32_t* counters = static_cast<uint32_t*>(workspace);
+  float* slots = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.counter_bytes);
+  switch (g.bn) {
+    case 16: return launch_proj<16>(wm, xm, ep, g, slots, counters, stream, pdl);
+    case 32: return launch_proj<32>(wm, xm, ep, g, slots, counters, stream, pdl);
+    case 64: return launch_proj<64>(wm, xm, ep, g, slots, counters, stream, pdl);
+    default: return launch_proj<128>(wm, xm, ep, g, slots, counters, stream, pdl);
+  }
+}
+
+}  // namespace npu_b200
+
+using namespace npu_b200;
+
+extern "C" size_t npu_b200_linear_workspace_size(int n_rows, int k, int batch) {
+  return proj_workspace_bytes(n_rows, k, batch);
+}
+
+extern "C" int npu_b200_linear(const void* d_x, const void* d_w, const void* d_bias, void* d_out,
+                               int batch, int n_rows, int k, int flags, void* d_workspace,
+                               size_t workspace_bytes, void* stream) {
+  clear_error();
+  NPU_REQUIRE((flags & ~(NPU_B200_LINEAR_RELU | NPU_B200_LINEAR_OUT_F32)) == 0,
+              "linear: unknown flags 0x%x", flags);
+  EpiParams ep;
+  ep.kind = kEpiStore;
+  ep.n_rows = n_rows;
+  ep.batch = batch;
+  ep.out = d_out;
+  ep.ld_out = n_rows;
+  ep.out_f32 = (flags & NPU_B200_LINEAR_OUT_F32) ? 1 : 0;
+  ep.relu = (flags & NPU_B200_LINEAR_RELU) ? 1 : 0;
+  ep.bias = static_cast<const __half*>(d_bias);
+  return proj_run(d_w, d_x, n_rows, k, batch, ep, d_workspace, workspace_bytes,
+                  static_cast<cudaStream_t>(stream), false);
+}

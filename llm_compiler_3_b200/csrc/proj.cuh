@@ -1,0 +1,73 @@
+// Projection (linear layer) kernel interface: D[n, b] = sum_k W[n, k] X[b, k]
+// on tcgen05 tensor cores, followed by one fused epilogue.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace npu_b200 {
+
+// What the epilogue does with the FP32 tile (128 weight rows x up to BN tokens).
+enum EpiKind : int {
+  kEpiStore = 0,   // out[b, n] = acc (+ bias[n]) (ReLU), FP16 or FP32
+  kEpiResid = 1,   // h = resid + acc; resid = h; xw = fp16(h * norm_w); ssq partial of h
+  kEpiSwiGLU = 2,  // rows [gate 64 | up 64] per tile: act[b, j] = silu(gate) * up
+  kEpiQKV = 3,     // per-head tiles: [QK-norm], RoPE, write q / append k,v to the cache
+  kEpiArgmax = 4,  // per-tile (max, argmax) over rows for every token
+};
+
+struct EpiParams {
+  int kind = kEpiStore;
+  int n_rows = 0;  // valid rows of W (N)
+  int batch = 0;   // valid tokens (columns)
+
+  // Optional RMSNorm scale of the input tokens: rn[b] = rsqrt(sum_p ssq_in[p][b] / hidden + eps),
+  // sum over `ssq_parts` partial sums written by the producer of X.
+  const float* ssq_in = nullptr;
+  int ssq_parts = 0;
+  int ssq_ld = 0;
+  float ssq_inv_hidden = 0.f;
+  float ssq_eps = 0.f;
+
+  // kEpiStore
+  void* out = nullptr;
+  int ld_out = 0;
+  int out_f32 = 0;
+  int relu = 0;
+  const __half* bias = nullptr;
+
+  // kEpiResid
+  float* resid = nullptr;
+  int ld_resid = 0;
+  const __half* norm_w = nullptr;
+  __half* xw = nullptr;
+  int ld_xw = 0;
+  float* ssq_out = nullptr;  // [tile][ssq_out_ld]
+  int ssq_out_ld = 0;
+
+  // kEpiQKV (head_dim 128: one tile is one head)
+  int q_heads = 0, kv_heads = 0;
+  const int32_t* positions = nullptr;
+  const float* inv_freq = nullptr;  // [64]
+  __half* k_cache = nullptr;        // [batch_cap][kv_heads][max_seq][128]
+  __half* v_cache = nullptr;
+  int max_seq = 0;
+  int cache_batch_stride = 0;       // elements between sequences of the cache = kv_heads*max_seq*128
+  const __half* q_norm_w = nullptr;
+  const __half* k_norm_w = nullptr;
+  float qk_eps = 0.f;
+
+  // kEpiArgmax: part_val/part_idx [tile][batch]
+  float* am_val = nullptr;
+  int32_t* am_idx = nullptr;
+  int am_ld = 0;
+};
+
+// Runs the projection.  w [n_rows, k] FP16 row-major, x [batch, k] FP16 row-major.
+// Workspace: proj_workspace_bytes(); zero-filled once, left zero-filled.
+int proj_run(const void* w, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
+             void* workspace, size_t workspace_bytes, cudaStream_t stream, bool pdl);
+size_t proj_workspace_bytes(int n_rows, int k, int batch);
+
+}  // namespace npu_b200

@@ -1,0 +1,188 @@
+// Small memory-bound kernels around the projections of a decode step.
+//
+//  * residual_update: the residual stream entering a layer stack or leaving an
+//    all-reduce.  h = source (embedding row, FP16 hidden state, or resid +
+//    all-reduced partial); resid = h (FP32); xw = fp16(h * norm_w); and one
+//    partial sum of squares of h per 128-row chunk and token, which the next
+//    projection turns into the RMSNorm scale in its epilogue
+//    (lib/Transforms/Pipeline.cpp:149-185: row reductions in FP32).
+//  * argmax_reduce / argmax_combine: greedy token choice over the per-tile
+//    (max, index) pairs the LM-head epilogue leaves, ties to the lowest id.
+//  * store_hidden: FP32 residual -> FP16 hidden-state output.
+#include <math.h>
+
+#include "common.cuh"
+#include "host.hpp"
+#include "small.cuh"
+
+namespace npu_b200 {
+namespace {
+
+constexpr int kChunk = 128;
+
+__global__ void __launch_bounds__(kChunk)
+    residual_update_kernel(ResidualUpdate p) {
+  pdl_wait();
+  __shared__ float red[kChunk / 32];
+  const int n = blockIdx.x * kChunk + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float w = __half2float(p.norm_w[n]);
+  if (blockIdx.x == 0 && p.positions && p.seq_lens)
+    for (int b = threadIdx.x; b < p.batch; b += blockDim.x) p.seq_lens[b] = p.positions[b] + 1;
+  for (int b = 0; b < p.batch; ++b) {
+    float h;
+    if (p.mode == kResidFromEmbedding) {
+      const int tok = p.tokens[b];
+      if (tok < 0 || tok >= p.vocab) {
+        if (threadIdx.x == 0) report_error(kDevErrBounds);
+        h = 0.f;
+      } else {
+        h = __half2float(p.embed[static_cast<size_t>(tok) * p.hidden + n]);
+      }
+    } else if (p.mode == kResidFromHidden) {
+      h = __half2float(p.hidden_in[static_cast<size_t>(b) * p.hidden + n]);
+    } else {
+      h = p.resid[static_cast<size_t>(b) * p.hidden + n] +
+          p.partial[static_cast<size_t>(b) * p.hidden + n];
+    }
+    p.resid[static_cast<size_t>(b) * p.hidden + n] = h;
+    p.xw[static_cast<size_t>(b) * p.hidden + n] = __float2half_rn(h * w);
+    float s = h * h;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+#pragma unroll
+      for (int i = 0; i < kChunk / 32; ++i) t += red[i];
+      p.ssq_out[static_cast<size_t>(blockIdx.x) * p.ssq_ld + b] = t;
+    }
+    __syncthreads();
+  }
+  pdl_launch_dependents();
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(256)
+    argmax_reduce_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
+                         int n_tiles, int ld, int id_offset, float* __restrict__ out_val,
+                         int32_t* __restrict__ out_idx) {
+  pdl_wait();
+  const int b = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
+    const float v = part_val[static_cast<size_t>(t) * ld + b];
+    const int i = part_idx[static_cast<size_t>(t) * ld + b];
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    out_val[b] = bv;
+    out_idx[b] = bi + id_offset;
+  }
+  pdl_launch_dependents();
+}
+
+// gathered: [ranks][2][ld] as {values; ids} per rank.
+__global__ void argmax_combine_kernel(const float* __restrict__ gathered, int ranks, int ld,
+                                      int batch, int32_t* __restrict__ out_ids) {
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < ranks; ++r) {
+      const float v = gathered[static_cast<size_t>(r) * 2 * ld + b];
+      const int i = __float_as_int(gathered[static_cast<size_t>(r) * 2 * ld + ld + b]);
+      if (better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+    out_ids[b] = bi;
+  }
+  pdl_launch_dependents();
+}
+
+__global__ void store_hidden_kernel(const float* __restrict__ resid, __half* __restrict__ out,
+                                    size_t count) {
+  pdl_wait();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = __float2half_rn(resid[i]);
+  pdl_launch_dependents();
+}
+
+}  // namespace
+
+int residual_update(const ResidualUpdate& p, cudaStream_t stream, bool pdl) {
+  NPU_REQUIRE(p.hidden % kChunk == 0 && p.batch >= 1 && p.batch <= 1024,
+              "residual update: hidden %d must be a multiple of 128", p.hidden);
+  LaunchCfg cfg;
+  cfg.grid = dim3(p.hidden / kChunk);
+  cfg.block = dim3(kChunk);
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, residual_update_kernel, p);
+}
+
+int argmax_reduce(const float* part_val, const int32_t* part_idx, int n_tiles, int ld, int batch,
+                  int id_offset, float* out_val, int32_t* out_idx, cudaStream_t stream, bool pdl) {
+  LaunchCfg cfg;
+  cfg.grid = dim3(batch);
+  cfg.block = dim3(256);
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, argmax_reduce_kernel, part_val, part_idx, n_tiles, ld, id_offset, out_val,
+                out_idx);
+}
+
+int argmax_combine(const float* gathered, int ranks, int ld, int batch, int32_t* out_ids,
+                   cudaStream_t stream, bool pdl) {
+  LaunchCfg cfg;
+  cfg.grid = dim3((batch + 127) / 128);
+  cfg.block = dim3(128);
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, argmax_combine_kernel, gathered, ranks, ld, batch, out_ids);
+}
+
+int store_hidden(const float* resid, __half* out, size_t count, cudaStream_t stream, bool pdl) {
+  LaunchCfg cfg;
+  cfg.grid = dim3(static_cast<unsigned>((count + 255) / 256 < 1184 ? (count + 255) / 256 : 1184));
+  cfg.block = dim3(256);
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, store_hidden_kernel, resid, out, count);
+}
+
+}  // namespace npu_b200

@@ -1,0 +1,41 @@
+// Interfaces of the small kernels in small.cu.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace npu_b200 {
+
+enum ResidualSource : int {
+  kResidFromEmbedding = 0,  // h = embed[tokens[b]]
+  kResidFromHidden = 1,     // h = hidden_in[b] (FP16)
+  kResidAddPartial = 2,     // h = resid[b] + partial[b] (after the all-reduce)
+};
+
+struct ResidualUpdate {
+  int mode = kResidFromEmbedding;
+  int batch = 0;
+  int hidden = 0;
+  int vocab = 0;
+  const int32_t* tokens = nullptr;
+  const __half* embed = nullptr;      // [vocab, hidden]
+  const __half* hidden_in = nullptr;  // [batch, hidden]
+  const float* partial = nullptr;     // [batch, hidden]
+  float* resid = nullptr;             // [batch, hidden]
+  const __half* norm_w = nullptr;     // [hidden] weight of the RMSNorm that follows
+  __half* xw = nullptr;               // [batch, hidden] fp16(h * norm_w)
+  float* ssq_out = nullptr;           // [hidden / 128][ssq_ld]
+  int ssq_ld = 0;
+  const int32_t* positions = nullptr; // optional: seq_lens[b] = positions[b] + 1
+  int32_t* seq_lens = nullptr;
+};
+
+int residual_update(const ResidualUpdate& p, cudaStream_t stream, bool pdl);
+int argmax_reduce(const float* part_val, const int32_t* part_idx, int n_tiles, int ld, int batch,
+                  int id_offset, float* out_val, int32_t* out_idx, cudaStream_t stream, bool pdl);
+int argmax_combine(const float* gathered, int ranks, int ld, int batch, int32_t* out_ids,
+                   cudaStream_t stream, bool pdl);
+int store_hidden(const float* resid, __half* out, size_t count, cudaStream_t stream, bool pdl);
+
+}  // namespace npu_b200

@@ -1,0 +1,80 @@
+"""tcgen05 projection kernel (npu_b200_linear) against the CPU oracle (GPU tests).
+
+The reference pins its matmul bit for bit on the 1/16 grid
+(test/Integration/matmul.py:18-26): every FP32 partial sum is exact there, so
+the FP16 result must match the oracle exactly whatever the summation order.
+Random operands are held to the north-star FP16 tolerance."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN, seeded
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(*ts):
+    return [t.to("cuda:0") for t in ts]
+
+
+@pytest.mark.parametrize("batch,n,k", [(1, 128, 64), (16, 256, 512), (64, 96, 512),
+                                       (5, 384, 448), (128, 128, 256), (33, 1000, 512)])
+def test_grid_values_bit_exact(cuda, batch, n, k):
+    from llm_compiler_3_b200 import _native, ops
+    x = oracle.grid_values(batch * k, 7).reshape(batch, k)
+    w = oracle.grid_values(n * k, 3).reshape(n, k)
+    xd, wd = _dev(x, w)
+    got = ops.linear(xd, wd).cpu()
+    assert _native.device_status() == 0
+    expected = oracle.linear(x, w).half()
+    assert torch.equal(got.view(torch.int16), expected.view(torch.int16))
+
+
+@pytest.mark.parametrize("batch", [1, 2, 16, 17, 64, 100])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (1024, 4096), (4096, 14336), (640, 1792)])
+def test_random_fp32_out(cuda, batch, n, k):
+    """Decode projection shapes (q/o 4096x4096, k/v 1024x4096, down 4096x14336, a
+    TP-8 shard) with outputs kept in FP32: stream-K splits of K across CTAs."""
+    from llm_compiler_3_b200 import _native, ops
+    x = seeded((batch, k), 100 + batch)
+    w = seeded((n, k), 200 + n, std=0.02)
+    xd, wd = _dev(x, w)
+    got = ops.linear(xd, wd, out_dtype=torch.float32).cpu()
+    assert _native.device_status() == 0
+    ref = oracle.linear(x, w)
+    err = float((got - ref).abs().max())
+    assert err < 2e-3 * float(ref.abs().max()) + 1e-4, err
+    assert oracle.cosine(got, ref) > 0.99999
+
+
+def test_deterministic_across_calls(cuda):
+    from llm_compiler_3_b200 import ops
+    x, w = _dev(seeded((64, 4096), 1), seeded((4096, 4096), 2, std=0.02))
+    first = ops.linear(x, w, out_dtype=torch.float32)
+    for _ in range(3):
+        assert torch.equal(ops.linear(x, w, out_dtype=torch.float32), first)
+
+
+def test_mlp_config_against_module(cuda):
+    """MLP config: batch 64, Linear 256->512 (+bias, ReLU) then 512->256 (+bias),
+    checked against the PyTorch module (examples/pytorch/mlp.py:44-61, rtol 0.01 of
+    the peak, mlp.py:37-38,88) and against the FP32 oracle."""
+    from llm_compiler_3_b200 import ops
+    z = {k: torch.from_numpy(v) for k, v in np.load(GOLDEN / "mlp.npz").items()}
+    x, w1, b1, w2, b2 = _dev(z["x"], z["w1"], z["b1"], z["w2"], z["b2"])
+    hidden = ops.linear(x, w1, b1, relu=True)
+    y = ops.linear(hidden, w2, b2).float().cpu()
+    expected = z["expected"]
+    assert float((y - expected).abs().max()) <= 0.01 * float(expected.abs().max())
+    ref = oracle.mlp_forward(z["x"], z["w1"], z["b1"], z["w2"], z["b2"])
+    assert float((y - ref).abs().max()) < 2e-2
+    assert oracle.cosine(y, ref) >= 0.9999
+
+
+def test_bad_shapes_rejected(cuda):
+    from llm_compiler_3_b200 import _native, ops
+    x = torch.zeros(4, 100, dtype=torch.float16, device="cuda:0")
+    w = torch.zeros(128, 100, dtype=torch.float16, device="cuda:0")
+    with pytest.raises(_native.NpuError, match="multiple of 64"):
+        ops.linear(x, w)
