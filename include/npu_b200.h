@@ -116,10 +116,75 @@ NPU_B200_API int npu_b200_flash_decode(const void* d_q, const void* d_k, const v
  *     zero-filled before first use and left zero-filled by every call. */
 #define NPU_B200_LINEAR_RELU 1
 #define NPU_B200_LINEAR_OUT_F32 2
+#define NPU_B200_LINEAR_PACKED_W 4 /* d_w is in the panel layout of npu_b200_pack_weight */
 NPU_B200_API size_t npu_b200_linear_workspace_size(int n_rows, int k, int batch);
 NPU_B200_API int npu_b200_linear(const void* d_x, const void* d_w, const void* d_bias, void* d_out,
                                  int batch, int n_rows, int k, int flags, void* d_workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* Weight panels: the B200 counterpart of the reference image builder's packed
+ * panels (lib/Transforms/Tile.cpp:351-395 packWeightPanels; hbm.bin layout
+ * [N/p][K][p], tools/npu-compile/npu-compile.cpp:637-648).  W [n_rows, k] becomes
+ * 16 KB blocks [ceil(n_rows/128)][k/64], each 128 rows x 64 columns in the
+ * 128-byte-swizzled K-major order the tensor cores read, so a projection streams
+ * every block with one contiguous bulk copy.  Rows past n_rows are zero. */
+NPU_B200_API size_t npu_b200_packed_weight_bytes(int n_rows, int k);
+NPU_B200_API int npu_b200_pack_weight(const void* d_w, int n_rows, int k, void* d_packed,
+                                      void* stream);
+
+/* Projection with a fused epilogue (the decode runtime's building block,
+ * exposed for kernel-level use and tests).  acc[b, n] = sum_k x[b, k] w[n, k]
+ * in FP32, times rn[b] = rsqrt(sum_p ssq_in[p * ssq_ld + b] / hidden + ssq_eps) when
+ * ssq_in is set (the RMSNorm of x, whose weight the producer of x applied), then:
+ *   STORE   out[b * ld_out + n] = act(acc + bias[n])                (FP16 or FP32)
+ *   RESID   h = resid[b * ld_resid + n] + acc; resid = h;
+ *           xw[b * ld_xw + n] = fp16(h * norm_w[n]);
+ *           ssq_out[(n / 128) * ssq_out_ld + b] = sum over the tile's rows of h^2
+ *   SWIGLU  rows in [gate 64 | up 64] blocks: out[b * ld_out + j] = silu(gate_j) * up_j
+ *   QKV     rows = [q_heads | kv_heads | kv_heads] x 128: optional per-head RMSNorm
+ *           (q_norm_w / k_norm_w, qk_eps), RoPE at positions[b] (inv_freq[64]),
+ *           q -> out[b * ld_out + head * 128 + d], k / v -> cache
+ *           [b][head][positions[b]][d] of [batch][kv_heads][max_seq][128]
+ *   ARGMAX  per 128-row tile: am_val / am_idx[tile * am_ld + b] = max / argmax of acc
+ *           over the tile's valid rows (lowest row on ties). */
+enum {
+  NPU_B200_EPI_STORE = 0,
+  NPU_B200_EPI_RESID = 1,
+  NPU_B200_EPI_SWIGLU = 2,
+  NPU_B200_EPI_QKV = 3,
+  NPU_B200_EPI_ARGMAX = 4
+};
+typedef struct npu_b200_epilogue {
+  int kind;
+  const float* ssq_in;
+  int ssq_parts, ssq_ld, hidden;
+  float ssq_eps;
+  void* out;
+  int ld_out, out_f32, relu;
+  const void* bias;
+  float* resid;
+  int ld_resid;
+  const void* norm_w;
+  void* xw;
+  int ld_xw;
+  float* ssq_out;
+  int ssq_out_ld;
+  int q_heads, kv_heads;
+  const int32_t* positions;
+  const float* inv_freq;
+  void* k_cache;
+  void* v_cache;
+  int max_seq;
+  const void* q_norm_w;
+  const void* k_norm_w;
+  float qk_eps;
+  float* am_val;
+  int32_t* am_idx;
+  int am_ld;
+} npu_b200_epilogue;
+NPU_B200_API int npu_b200_projection(const void* d_x, const void* d_w, int w_packed, int batch,
+                                     int n_rows, int k, const npu_b200_epilogue* epilogue,
+                                     void* d_workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Decode runtime (context-level).

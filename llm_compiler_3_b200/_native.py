@@ -53,6 +53,10 @@ _SIGNATURES = [
     ("npu_b200_linear", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
       c_void_p]),
+    ("npu_b200_packed_weight_bytes", c_size_t, [c_int, c_int]),
+    ("npu_b200_pack_weight", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    ("npu_b200_projection", c_int,
+     [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("npu_b200_nccl_unique_id", c_int, [c_void_p]),
     ("npu_b200_create", c_int, [c_int, c_int, c_int, c_void_p, POINTER(c_void_p)]),
     ("npu_b200_destroy", c_int, [c_void_p]),
@@ -72,6 +76,24 @@ _SIGNATURES = [
 
 LINEAR_RELU = 1
 LINEAR_OUT_F32 = 2
+LINEAR_PACKED_W = 4
+
+EPI_STORE, EPI_RESID, EPI_SWIGLU, EPI_QKV, EPI_ARGMAX = range(5)
+
+
+class Epilogue(ctypes.Structure):
+    """Mirror of npu_b200_epilogue (include/npu_b200.h)."""
+
+    _fields_ = [
+        ("kind", c_int), ("ssq_in", c_void_p), ("ssq_parts", c_int), ("ssq_ld", c_int),
+        ("hidden", c_int), ("ssq_eps", c_float), ("out", c_void_p), ("ld_out", c_int),
+        ("out_f32", c_int), ("relu", c_int), ("bias", c_void_p), ("resid", c_void_p),
+        ("ld_resid", c_int), ("norm_w", c_void_p), ("xw", c_void_p), ("ld_xw", c_int),
+        ("ssq_out", c_void_p), ("ssq_out_ld", c_int), ("q_heads", c_int), ("kv_heads", c_int),
+        ("positions", c_void_p), ("inv_freq", c_void_p), ("k_cache", c_void_p),
+        ("v_cache", c_void_p), ("max_seq", c_int), ("q_norm_w", c_void_p), ("k_norm_w", c_void_p),
+        ("qk_eps", c_float), ("am_val", c_void_p), ("am_idx", c_void_p), ("am_ld", c_int),
+    ]
 
 _lib = None
 

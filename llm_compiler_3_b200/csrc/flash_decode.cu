@@ -27,6 +27,10 @@ namespace {
 constexpr int kKeysPerTile = 32;  // keys per warp stage
 constexpr int kMaxGroup = 8;      // query heads per KV head (MMA N)
 constexpr int kMaxSplits = 256;   // merge statistics of all splits fit in shared memory
+// Split counters occupy a fixed region at the start of the workspace, whatever
+// the batch, so one workspace serves every batch size.
+constexpr int kMaxUnits = 16384;  // sequences x KV heads
+constexpr size_t kCounterBytes = kMaxUnits * sizeof(uint32_t);
 
 template <int D>
 struct FdShape {
@@ -73,6 +77,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   __syncwarp();
 
+  // The next kernel may be scheduled once every CTA of this grid is resident;
+  // it waits for this grid's results itself.
+  pdl_launch_dependents();
   // Everything below reads what the previous kernel (the KV append) wrote.
   pdl_wait();
 
@@ -258,7 +265,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
   }
 
-  pdl_launch_dependents();
   __syncthreads();  // every warp is done with its stages: reuse them for the merge
 
   // Per-warp results: cm/cl [WARPS][8], co [WARPS][8][D].
@@ -415,7 +421,7 @@ int resolve_splits(int batch, int kv_heads, int max_seq, int num_splits, int* kp
 size_t workspace_bytes_for(int batch, int kv_heads, int head_dim, int splits) {
   if (splits <= 1) return 0;
   const size_t units = static_cast<size_t>(batch) * kv_heads;
-  const size_t counters = (units * sizeof(uint32_t) + 255) / 256 * 256;
+  const size_t counters = kCounterBytes;
   const size_t part_floats = static_cast<size_t>(kMaxGroup) * head_dim + 2 * kMaxGroup;
   return counters + units * splits * part_floats * sizeof(float);
 }
@@ -454,6 +460,8 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
   NPU_REQUIRE(head_dim == 64 || head_dim == 128, "flash_decode: head_dim %d not in {64,128}",
               head_dim);
   NPU_REQUIRE(max_seq >= 1, "flash_decode: max_seq %d", max_seq);
+  NPU_REQUIRE(batch * kv_heads <= kMaxUnits, "flash_decode: batch x kv_heads exceeds %d",
+              kMaxUnits);
   NPU_REQUIRE(static_cast<long long>(batch) * kv_heads * max_seq < (1ll << 31),
               "flash_decode: cache has too many rows for 32-bit TMA coordinates");
   NPU_REQUIRE(std::isfinite(scale), "flash_decode: scale is not finite");
@@ -478,9 +486,9 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
 
   const size_t units = static_cast<size_t>(batch) * kv_heads;
   uint32_t* counters = reinterpret_cast<uint32_t*>(workspace);
-  float* part = need ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
-                                                (units * sizeof(uint32_t) + 255) / 256 * 256)
-                     : nullptr;
+  float* part =
+      need ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kCounterBytes)
+           : nullptr;
   const float scale_log2 = scale * 1.4426950408889634f;
   const __half* qh = static_cast<const __half*>(q);
   __half* oh = static_cast<__half*>(out);

@@ -19,6 +19,7 @@
 // warp 4 TMA producer, warp 5 MMA issuer.  Two TMEM accumulators let the MMA of
 // the next tile overlap the epilogue of the previous one.
 #include <math.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "host.hpp"
@@ -29,8 +30,16 @@ namespace {
 
 constexpr int kEpiThreads = 128;
 constexpr int kThreads = 192;
-constexpr int kMaxStages = 12;
-constexpr int kSmemBudget = 232448;  // 227 KB opt-in limit per block
+constexpr int kMaxStages = 8;
+constexpr int kCtasPerSm = 2;        // one CTA streams while the other finishes its epilogue
+constexpr int kSmemPerSm = 233472;   // 228 KB of shared memory per SM
+constexpr int kSmemReserved = 1024;  // per-CTA system reservation
+constexpr int kChunkCols = 16;       // tokens per epilogue chunk (one tcgen05.ld x16)
+// Tile counters sit in a fixed-size region at the start of the workspace, so
+// projections of different shapes can share one workspace: a counter is never
+// overlapped by another shape's partial-sum slots.
+constexpr int kMaxTiles = 16384;
+constexpr size_t kCounterBytes = kMaxTiles * sizeof(uint32_t);
 
 template <int BN>
 struct ProjShape {
@@ -38,7 +47,7 @@ struct ProjShape {
   static constexpr int kBBytes = BN * 64 * 2;   // one BN-token x 64-k activation block
   static constexpr int kStageBytes = (kABytes + kBBytes + 1023) / 1024 * 1024;
   static constexpr int kPitch = 128 + 4;        // floats per token column of the epilogue tile
-  static constexpr int kTileBytes = kPitch * BN * 4;
+  static constexpr int kTileBytes = kPitch * kChunkCols * 4;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kMiscBytes = 512 + 8 * BN;  // barriers, TMEM slot, per-token scalars
 };
@@ -74,23 +83,26 @@ __device__ __forceinline__ int owner_cta(long long i, long long total, int grid)
   return static_cast<int>(c);
 }
 
-template <int BN>
-__device__ __forceinline__ void run_epilogue(const EpiParams& ep, int tile, int r, float (&v)[BN],
-                                             const float* rn, float* tile_s, float* aux) {
-  using S = ProjShape<BN>;
-  constexpr int P = S::kPitch;
+// Epilogue of one 16-token chunk of a finished 128-row tile.  Thread r holds
+// row tile*128 + r for tokens b0 .. b0+15 in v[].  All branches depend only on
+// the tile and the chunk, so every epilogue thread reaches the same barriers.
+__device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile, int r, int b0,
+                                                   float (&v)[kChunkCols], const float* rn,
+                                                   float* tile_s, float* aux, const int* pos_s) {
+  constexpr int P = 128 + 4;
   const int batch = ep.batch;
 #pragma unroll
-  for (int b = 0; b < BN; ++b) v[b] *= rn[b];
+  for (int q = 0; q < kChunkCols; ++q) v[q] *= rn[b0 + q];
 
   if (ep.kind == kEpiStore) {
     const int n = tile * 128 + r;
     if (n < ep.n_rows) {
       const float bias = ep.bias ? __half2float(ep.bias[n]) : 0.f;
 #pragma unroll
-      for (int b = 0; b < BN; ++b) {
+      for (int q = 0; q < kChunkCols; ++q) {
+        const int b = b0 + q;
         if (b < batch) {
-          float val = v[b] + bias;
+          float val = v[q] + bias;
           if (ep.relu) val = fmaxf(val, 0.f);
           const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
           if (ep.out_f32)
@@ -104,36 +116,50 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& ep, int tile, int 
     const int n = tile * 128 + r;
     const bool valid = n < ep.n_rows;
     const float w = valid ? __half2float(ep.norm_w[n]) : 0.f;
+    // Independent loads first: the chunk costs one memory round trip.
+    float rv[kChunkCols];
 #pragma unroll
-    for (int b = 0; b < BN; ++b) {
+    for (int q = 0; q < kChunkCols; ++q) {
+      const int b = b0 + q;
+      rv[q] = (valid && b < batch) ? __ldcg(ep.resid + static_cast<size_t>(b) * ep.ld_resid + n)
+                                   : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < kChunkCols; ++q) {
+      const int b = b0 + q;
       float h2 = 0.f;
       if (valid && b < batch) {
-        float* rp = ep.resid + static_cast<size_t>(b) * ep.ld_resid + n;
-        const float h = *rp + v[b];
-        *rp = h;
+        const float h = rv[q] + v[q];
+        ep.resid[static_cast<size_t>(b) * ep.ld_resid + n] = h;
         ep.xw[static_cast<size_t>(b) * ep.ld_xw + n] = __float2half_rn(h * w);
         h2 = h * h;
       }
-      tile_s[b * P + r] = h2;
+      tile_s[q * P + r] = h2;
     }
     epi_sync();
-    if (r < batch) {
+    if (r < kChunkCols && b0 + r < batch) {
       float s = 0.f;
+#pragma unroll 8
       for (int i = 0; i < 128; ++i) s += tile_s[r * P + i];
-      ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + r] = s;
+      ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + b0 + r] = s;
     }
     epi_sync();
   } else if (ep.kind == kEpiSwiGLU) {
 #pragma unroll
-    for (int b = 0; b < BN; ++b) tile_s[b * P + r] = v[b];
+    for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = v[q];
     epi_sync();
     const int j = tile * 64 + r;
     if (r < 64 && j < ep.n_rows / 2) {
-      for (int b = 0; b < batch; ++b) {
-        const float g = tile_s[b * P + r];
-        const float u = tile_s[b * P + r + 64];
-        const float act = g / (1.f + expf(-g)) * u;
-        static_cast<__half*>(ep.out)[static_cast<size_t>(b) * ep.ld_out + j] = __float2half_rn(act);
+#pragma unroll
+      for (int q = 0; q < kChunkCols; ++q) {
+        const int b = b0 + q;
+        if (b < batch) {
+          const float g = tile_s[q * P + r];
+          const float u = tile_s[q * P + r + 64];
+          const float act = g / (1.f + expf(-g)) * u;
+          static_cast<__half*>(ep.out)[static_cast<size_t>(b) * ep.ld_out + j] =
+              __float2half_rn(act);
+        }
       }
     }
     epi_sync();
@@ -143,53 +169,55 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& ep, int tile, int 
     const __half* nw = is_q ? ep.q_norm_w : (is_k ? ep.k_norm_w : nullptr);
     if (nw) {  // per-head RMSNorm over the 128 dims (Qwen3 q_norm / k_norm)
 #pragma unroll
-      for (int b = 0; b < BN; ++b) tile_s[b * P + r] = v[b] * v[b];
+      for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = v[q] * v[q];
       epi_sync();
-      if (r < BN) {
+      if (r < kChunkCols) {
         float s = 0.f;
+#pragma unroll 8
         for (int i = 0; i < 128; ++i) s += tile_s[r * P + i];
         aux[r] = rsqrtf(s * (1.f / 128.f) + ep.qk_eps);
       }
       epi_sync();
       const float wr = __half2float(nw[r]);
 #pragma unroll
-      for (int b = 0; b < BN; ++b) v[b] = v[b] * aux[b] * wr;
+      for (int q = 0; q < kChunkCols; ++q) v[q] = v[q] * aux[q] * wr;
     }
     if (is_q || is_k) {  // RoPE: rotate_half pairs (i, i + 64)
 #pragma unroll
-      for (int b = 0; b < BN; ++b) tile_s[b * P + r] = v[b];
+      for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = v[q];
       epi_sync();
       const float f = ep.inv_freq[r & 63];
 #pragma unroll
-      for (int b = 0; b < BN; ++b) {
-        if (b < batch) {
-          const float partner = tile_s[b * P + (r ^ 64)];
-          const float theta = static_cast<float>(ep.positions[b]) * f;
+      for (int q = 0; q < kChunkCols; ++q) {
+        if (b0 + q < batch) {
+          const float partner = tile_s[q * P + (r ^ 64)];
+          const float theta = static_cast<float>(pos_s[b0 + q]) * f;
           float sn, cs;
           sincosf(theta, &sn, &cs);
-          v[b] = r < 64 ? v[b] * cs - partner * sn : v[b] * cs + partner * sn;
+          v[q] = r < 64 ? v[q] * cs - partner * sn : v[q] * cs + partner * sn;
         }
       }
       epi_sync();
     }
     if (is_q) {
-      __half* q = static_cast<__half*>(ep.out);
+      __half* qo = static_cast<__half*>(ep.out);
 #pragma unroll
-      for (int b = 0; b < BN; ++b)
-        if (b < batch)
-          q[static_cast<size_t>(b) * ep.ld_out + tile * 128 + r] = __float2half_rn(v[b]);
+      for (int q = 0; q < kChunkCols; ++q)
+        if (b0 + q < batch)
+          qo[static_cast<size_t>(b0 + q) * ep.ld_out + tile * 128 + r] = __float2half_rn(v[q]);
     } else {
       const int kh = is_k ? tile - ep.q_heads : tile - ep.q_heads - ep.kv_heads;
       __half* cache = is_k ? ep.k_cache : ep.v_cache;
 #pragma unroll
-      for (int b = 0; b < BN; ++b) {
+      for (int q = 0; q < kChunkCols; ++q) {
+        const int b = b0 + q;
         if (b < batch) {
-          const int pos = ep.positions[b];
+          const int pos = pos_s[b];
           if (pos < 0 || pos >= ep.max_seq) {
             if (r == 0) report_error(kDevErrBounds);
           } else {
             cache[static_cast<size_t>(b) * ep.cache_batch_stride +
-                  (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + r] = __float2half_rn(v[b]);
+                  (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + r] = __float2half_rn(v[q]);
           }
         }
       }
@@ -198,9 +226,9 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& ep, int tile, int 
     const int n = tile * 128 + r;
     const bool valid = n < ep.n_rows;
 #pragma unroll
-    for (int b = 0; b < BN; ++b) tile_s[b * P + r] = valid ? v[b] : -INFINITY;
+    for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = valid ? v[q] : -INFINITY;
     epi_sync();
-    if (r < batch) {
+    if (r < kChunkCols && b0 + r < batch) {
       float best = -INFINITY;
       int bi = tile * 128;
       for (int i = 0; i < 128; ++i) {
@@ -210,18 +238,19 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& ep, int tile, int 
           bi = tile * 128 + i;
         }
       }
-      ep.am_val[static_cast<size_t>(tile) * ep.am_ld + r] = best;
-      ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + r] = bi;
+      ep.am_val[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = best;
+      ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = bi;
     }
     epi_sync();
   }
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                const __grid_constant__ EpiParams ep, int n_tiles, int kblocks, int stages,
-                float* __restrict__ slots, uint32_t* __restrict__ counters) {
+                const __grid_constant__ EpiParams ep, const uint8_t* __restrict__ w_packed,
+                int n_tiles, int kblocks, int stages, float* __restrict__ slots,
+                uint32_t* __restrict__ counters) {
   using S = ProjShape<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
@@ -233,14 +262,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   float* rn = reinterpret_cast<float*>(tmem_slot + 4);  // [BN] input RMSNorm scale per token
-  float* aux = rn + BN;                                  // [BN] per-token scratch
-  volatile int* flags = reinterpret_cast<volatile int*>(aux + BN);  // [0] abort, [1] last
+  int* pos_s = reinterpret_cast<int*>(rn + BN);         // [BN] token positions (QKV)
+  float* aux = reinterpret_cast<float*>(pos_s + BN);    // [16] per-token scratch of a chunk
+  volatile int* flags = reinterpret_cast<volatile int*>(aux + kChunkCols);  // abort, last
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(n_tiles) * kblocks;
   const int grid = gridDim.x, cta = blockIdx.x;
   const long long it_begin = static_cast<long long>(cta) * total / grid;
   const long long it_end = static_cast<long long>(cta + 1) * total / grid;
+
+  // The next kernel may be scheduled as soon as every CTA of this one is
+  // resident; it waits for this grid's results itself (griddepcontrol.wait).
+  pdl_launch_dependents();
 
   if (warp == 4 && lane == 0) {
     prefetch_tensormap(&wmap);
@@ -273,14 +307,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_w = policy_evict_first();
       const int n_iter = static_cast<int>(it_end - it_begin);
       const int pre = min(stages, n_iter);
+      // Packed weights: iteration `it` is the contiguous 16 KB panel `it`.
+      auto load_w = [&](uint8_t* st, uint64_t* bar, long long it) {
+        if (w_packed != nullptr) {
+          bulk_load_hint(st, w_packed + static_cast<size_t>(it) * S::kABytes, S::kABytes, bar,
+                         pol_w);
+        } else {
+          const int tile = static_cast<int>(it / kblocks), kb = static_cast<int>(it % kblocks);
+          tma_load_2d_hint(st, &wmap, bar, kb * 64, tile * 128, pol_w);
+        }
+      };
       // Weights do not depend on the previous kernel: start streaming them
       // before waiting for it; the activations follow once it has finished.
       for (int i = 0; i < pre; ++i) {
-        const long long it = it_begin + i;
-        const int tile = static_cast<int>(it / kblocks), kb = static_cast<int>(it % kblocks);
         uint8_t* st = smem + i * S::kStageBytes;
         mbar_arrive_expect_tx(&full[i], S::kABytes + S::kBBytes);
-        tma_load_2d_hint(st, &wmap, &full[i], kb * 64, tile * 128, pol_w);
+        load_w(st, &full[i], it_begin + i);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
@@ -295,10 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const long long it = it_begin + i;
-        const int tile = static_cast<int>(it / kblocks), kb = static_cast<int>(it % kblocks);
+        const int kb = static_cast<int>(it % kblocks);
         uint8_t* st = smem + s * S::kStageBytes;
         mbar_arrive_expect_tx(&full[s], S::kABytes + S::kBBytes);
-        tma_load_2d_hint(st, &wmap, &full[s], kb * 64, tile * 128, pol_w);
+        load_w(st, &full[s], it);
         tma_load_2d(st + S::kABytes, &xmap, &full[s], kb * 64, 0);
         issued = i + 1;
       }
@@ -361,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         scale = rsqrtf(s * ep.ssq_inv_hidden + ep.ssq_eps);
       }
       rn[r] = scale;
+      pos_s[r] = (ep.positions != nullptr && r < ep.batch) ? ep.positions[r] : 0;
     }
     epi_sync();
     long long it = it_begin;
@@ -376,27 +419,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float v[BN];
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + acc * BN;
-#pragma unroll
-      for (int j = 0; j < BN / 16; ++j) {
-        uint32_t rr[16];
-        tmem_ld16(taddr + j * 16, rr);
-        tmem_ld_wait();
-#pragma unroll
-        for (int q = 0; q < 16; ++q) v[j * 16 + q] = __uint_as_float(rr[q]);
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
-
       const bool whole = kb0 == 0 && seg_end == static_cast<long long>(tile + 1) * kblocks;
-      bool mine = true;
-      if (!whole) {
-        // Stream-K fix-up: publish this CTA's partial; the last contributor
-        // adds all of them in CTA order.  Slot index tile + cta is unique.
-        float* slot = slots + static_cast<size_t>(tile + cta) * 128 * BN;
+      if (whole) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
+          uint32_t rr[16];
+          tmem_ld16(taddr + c0, rr);
+          tmem_ld_wait();
+          float v[kChunkCols];
 #pragma unroll
-        for (int b = 0; b < BN; ++b) __stcg(slot + b * 128 + r, v[b]);
+          for (int q = 0; q < kChunkCols; ++q) v[q] = __uint_as_float(rr[q]);
+          run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      } else {
+        // Stream-K fix-up: publish this CTA's partial (slot tile + cta is
+        // unique), release the accumulator, and let the last contributor of
+        // the tile add every partial in CTA order (deterministic).
+        float* slot = slots + static_cast<size_t>(tile + cta) * 128 * BN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
+          uint32_t rr[16];
+          tmem_ld16(taddr + c0, rr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < kChunkCols; ++q) __stcg(slot + (c0 + q) * 128 + r, __uint_as_float(rr[q]));
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
         __threadfence();
         epi_sync();
         const int cf = owner_cta(static_cast<long long>(tile) * kblocks, total, grid);
@@ -406,34 +458,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           flags[1] = (prev == static_cast<uint32_t>(cl - cf)) ? 1 : 0;
         }
         epi_sync();
-        mine = flags[1] != 0;
-        if (mine) {
+        if (flags[1]) {
           __threadfence();
-          float sum[BN];
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
+            float v[kChunkCols];
 #pragma unroll
-          for (int b = 0; b < BN; ++b) sum[b] = 0.f;
-          for (int c = cf; c <= cl; ++c) {
-            if (c == cta) {
+            for (int q = 0; q < kChunkCols; ++q) v[q] = 0.f;
+            for (int c = cf; c <= cl; ++c) {
+              const float* other = slots + static_cast<size_t>(tile + c) * 128 * BN + c0 * 128 + r;
 #pragma unroll
-              for (int b = 0; b < BN; ++b) sum[b] += v[b];
-            } else {
-              const float* other = slots + static_cast<size_t>(tile + c) * 128 * BN;
-#pragma unroll
-              for (int b = 0; b < BN; ++b) sum[b] += __ldcg(other + b * 128 + r);
+              for (int q = 0; q < kChunkCols; ++q) v[q] += __ldcg(other + q * 128);
             }
+            run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s);
           }
-#pragma unroll
-          for (int b = 0; b < BN; ++b) v[b] = sum[b];
           if (r == 0) counters[tile] = 0u;  // leave the workspace reusable
         }
+        epi_sync();  // flags[1] is rewritten by the next fix-up
       }
-      if (mine) run_epilogue<BN>(ep, tile, r, v, rn, tile_s, aux);
       it = seg_end;
       ++seg;
     }
   }
 
-  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {
@@ -445,8 +492,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN>
 int stages_for() {
   using S = ProjShape<BN>;
+  const int budget = kSmemPerSm / kCtasPerSm - kSmemReserved;
   const int fixed = 1024 + S::kTileBytes + S::kMiscBytes;
-  int st = (kSmemBudget - fixed) / S::kStageBytes;
+  int st = (budget - fixed) / S::kStageBytes;
   return st > kMaxStages ? kMaxStages : st;
 }
 
@@ -469,16 +517,17 @@ Geometry geometry(int n_rows, int k, int batch) {
   g.n_tiles = (n_rows + 127) / 128;
   g.kblocks = k / 64;
   const long long total = static_cast<long long>(g.n_tiles) * g.kblocks;
-  g.grid = static_cast<int>(total < sm_count() ? total : sm_count());
-  g.counter_bytes = (static_cast<size_t>(g.n_tiles) * 4 + 255) / 256 * 256;
+  const long long slots_total = static_cast<long long>(sm_count()) * kCtasPerSm;
+  g.grid = static_cast<int>(total < slots_total ? total : slots_total);
+  g.counter_bytes = kCounterBytes;
   g.slot_bytes = static_cast<size_t>(g.n_tiles + g.grid - 1) * 128 * g.bn * 4;
   return g;
 }
 
 template <int BN>
 int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& ep,
-                const Geometry& g, float* slots, uint32_t* counters, cudaStream_t stream,
-                bool pdl) {
+                const uint8_t* w_packed, const Geometry& g, float* slots, uint32_t* counters,
+                cudaStream_t stream, bool pdl) {
   const int stages = stages_for<BN>();
   const size_t smem = smem_for<BN>(stages);
   auto kern = proj_kernel<BN>;
@@ -490,7 +539,27 @@ int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& e
   cfg.smem = smem;
   cfg.stream = stream;
   cfg.pdl = pdl;
-  return launch(cfg, kern, wm, xm, ep, g.n_tiles, g.kblocks, stages, slots, counters);
+  return launch(cfg, kern, wm, xm, ep, w_packed, g.n_tiles, g.kblocks, stages, slots, counters);
+}
+
+// One thread per 16-byte chunk of the source: row i, chunk c (elements 8c..8c+7)
+// goes to panel (tile, kb) = (row / 128, c / 8), row r = row % 128, chunk slot
+// (c % 8) ^ (r % 8): the layout TMA's 128-byte swizzle would leave in shared
+// memory, so a plain bulk copy of the panel feeds the MMA directly.
+__global__ void pack_panels_kernel(const __half* __restrict__ src, size_t src_pitch,
+                                   int n_src_rows, int k, uint8_t* __restrict__ dst, int kblocks,
+                                   int row_mode, int row_offset) {
+  const int chunks = k / 8;
+  const size_t total = static_cast<size_t>(n_src_rows) * chunks;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx / chunks), c = static_cast<int>(idx % chunks);
+    const int row = row_mode == 0 ? row_offset + i : (i / 64) * 128 + (i % 64) + row_offset;
+    const int t = row >> 7, r = row & 127, kb = c >> 3, j = c & 7;
+    const size_t off = (static_cast<size_t>(t) * kblocks + kb) * 16384 + r * 128 + ((j ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst + off) =
+        *reinterpret_cast<const uint4*>(src + static_cast<size_t>(i) * src_pitch + 8 * c);
+  }
 }
 
 }  // namespace
@@ -501,13 +570,42 @@ size_t proj_workspace_bytes(int n_rows, int k, int batch) {
   return g.counter_bytes + g.slot_bytes;
 }
 
-int proj_run(const void* w, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
-             void* workspace, size_t workspace_bytes, cudaStream_t stream, bool pdl) {
+size_t packed_weight_bytes(int n_rows, int k) {
+  if (n_rows < 1 || k < 64) return 0;
+  return static_cast<size_t>((n_rows + 127) / 128) * 128 * k * 2;
+}
+
+int pack_weight(const void* src, size_t src_pitch, int n_src_rows, int k, void* dst,
+                int dst_rows, int row_mode, int row_offset, cudaStream_t stream) {
+  NPU_REQUIRE(src && dst, "pack: null pointer");
+  NPU_REQUIRE(k >= 64 && k % 64 == 0 && n_src_rows >= 1 && src_pitch >= static_cast<size_t>(k),
+              "pack: K must be a positive multiple of 64 (K=%d)", k);
+  NPU_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (src_pitch * 2) % 16 == 0 &&
+                  (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
+              "pack: source rows and destination must be 16-byte aligned");
+  const int last = row_mode == 0 ? row_offset + n_src_rows - 1
+                                 : ((n_src_rows - 1) / 64) * 128 + ((n_src_rows - 1) % 64) + row_offset;
+  NPU_REQUIRE(row_offset >= 0 && last < ((dst_rows + 127) / 128) * 128,
+              "pack: rows land outside the destination");
+  LaunchCfg cfg;
+  const size_t total = static_cast<size_t>(n_src_rows) * (k / 8);
+  cfg.grid = dim3(static_cast<unsigned>(total / 256 + 1 < 4096 ? total / 256 + 1 : 4096));
+  cfg.block = dim3(256);
+  cfg.stream = stream;
+  return launch(cfg, pack_panels_kernel, static_cast<const __half*>(src), src_pitch, n_src_rows, k,
+                static_cast<uint8_t*>(dst), k / 64, row_mode, row_offset);
+}
+
+int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int batch,
+             const EpiParams& ep, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+             bool pdl) {
   NPU_REQUIRE(w && x, "projection: null weight or activation pointer");
   NPU_REQUIRE(n_rows >= 1 && k >= 64 && k % 64 == 0,
               "projection: need rows >= 1 and K a positive multiple of 64 (rows=%d K=%d)", n_rows,
               k);
   NPU_REQUIRE(batch >= 1 && batch <= 128, "projection: batch %d not in [1, 128]", batch);
+  NPU_REQUIRE((n_rows + 127) / 128 <= kMaxTiles, "projection: %d rows exceed %d tiles", n_rows,
+              kMaxTiles);
   NPU_REQUIRE(ep.batch == batch && ep.n_rows == n_rows, "projection: epilogue shape mismatch");
   NPU_REQUIRE((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
               "projection: W and X must be 16-byte aligned");
@@ -522,6 +620,10 @@ int proj_run(const void* w, const void* x, int n_rows, int k, int batch, const E
                 "projection: residual epilogue needs resid, norm weight, xw and ssq outputs");
   if (ep.kind == kEpiArgmax) NPU_REQUIRE(ep.am_val && ep.am_idx, "projection: argmax outputs");
   if (ep.kind == kEpiStore) NPU_REQUIRE(ep.out != nullptr, "projection: null output");
+  NPU_REQUIRE(ep.kind >= kEpiStore && ep.kind <= kEpiArgmax, "projection: unknown epilogue %d",
+              ep.kind);
+  NPU_REQUIRE(ep.ssq_in == nullptr || (ep.ssq_parts >= 1 && ep.ssq_ld >= batch),
+              "projection: RMSNorm input needs ssq_parts >= 1 and ssq_ld >= batch");
 
   const Geometry g = geometry(n_rows, k, batch);
   const size_t need = g.counter_bytes + g.slot_bytes;
@@ -530,17 +632,20 @@ int proj_run(const void* w, const void* x, int n_rows, int k, int batch, const E
   NPU_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
               "projection: workspace must be 256-byte aligned");
   CUtensorMap wm, xm;
-  int rc = make_tensor_map_2d(&wm, w, n_rows, k, 128, 64);
-  if (rc) return rc;
-  rc = make_tensor_map_2d(&xm, x, batch, k, g.bn, 64);
-  if (rc) return rc;
+  int rc = 0;
+  if (w_packed)
+    memset(&wm, 0, sizeof(wm));
+  else if ((rc = make_tensor_map_2d(&wm, w, n_rows, k, 128, 64)))
+    return rc;
+  if ((rc = make_tensor_map_2d(&xm, x, batch, k, g.bn, 64))) return rc;
   uint32_t* counters = static_cast<uint32_t*>(workspace);
   float* slots = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.counter_bytes);
+  const uint8_t* wp = w_packed ? static_cast<const uint8_t*>(w) : nullptr;
   switch (g.bn) {
-    case 16: return launch_proj<16>(wm, xm, ep, g, slots, counters, stream, pdl);
-    case 32: return launch_proj<32>(wm, xm, ep, g, slots, counters, stream, pdl);
-    case 64: return launch_proj<64>(wm, xm, ep, g, slots, counters, stream, pdl);
-    default: return launch_proj<128>(wm, xm, ep, g, slots, counters, stream, pdl);
+    case 16: return launch_proj<16>(wm, xm, ep, wp, g, slots, counters, stream, pdl);
+    case 32: return launch_proj<32>(wm, xm, ep, wp, g, slots, counters, stream, pdl);
+    case 64: return launch_proj<64>(wm, xm, ep, wp, g, slots, counters, stream, pdl);
+    default: return launch_proj<128>(wm, xm, ep, wp, g, slots, counters, stream, pdl);
   }
 }
 
@@ -552,11 +657,25 @@ extern "C" size_t npu_b200_linear_workspace_size(int n_rows, int k, int batch) {
   return proj_workspace_bytes(n_rows, k, batch);
 }
 
+extern "C" size_t npu_b200_packed_weight_bytes(int n_rows, int k) {
+  return packed_weight_bytes(n_rows, k);
+}
+
+extern "C" int npu_b200_pack_weight(const void* d_w, int n_rows, int k, void* d_packed,
+                                    void* stream) {
+  clear_error();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  NPU_REQUIRE(d_packed, "pack: null destination");
+  NPU_TRY_CUDA(cudaMemsetAsync(d_packed, 0, packed_weight_bytes(n_rows, k), s));
+  return pack_weight(d_w, static_cast<size_t>(k), n_rows, k, d_packed, n_rows, 0, 0, s);
+}
+
 extern "C" int npu_b200_linear(const void* d_x, const void* d_w, const void* d_bias, void* d_out,
                                int batch, int n_rows, int k, int flags, void* d_workspace,
                                size_t workspace_bytes, void* stream) {
   clear_error();
-  NPU_REQUIRE((flags & ~(NPU_B200_LINEAR_RELU | NPU_B200_LINEAR_OUT_F32)) == 0,
+  NPU_REQUIRE((flags & ~(NPU_B200_LINEAR_RELU | NPU_B200_LINEAR_OUT_F32 |
+                         NPU_B200_LINEAR_PACKED_W)) == 0,
               "linear: unknown flags 0x%x", flags);
   EpiParams ep;
   ep.kind = kEpiStore;
@@ -567,6 +686,51 @@ extern "C" int npu_b200_linear(const void* d_x, const void* d_w, const void* d_b
   ep.out_f32 = (flags & NPU_B200_LINEAR_OUT_F32) ? 1 : 0;
   ep.relu = (flags & NPU_B200_LINEAR_RELU) ? 1 : 0;
   ep.bias = static_cast<const __half*>(d_bias);
-  return proj_run(d_w, d_x, n_rows, k, batch, ep, d_workspace, workspace_bytes,
+  return proj_run(d_w, (flags & NPU_B200_LINEAR_PACKED_W) != 0, d_x, n_rows, k, batch, ep,
+                  d_workspace, workspace_bytes, static_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int npu_b200_projection(const void* d_x, const void* d_w, int w_packed, int batch,
+                                   int n_rows, int k, const npu_b200_epilogue* e, void* d_workspace,
+                                   size_t workspace_bytes, void* stream) {
+  clear_error();
+  NPU_REQUIRE(e != nullptr, "projection: null epilogue");
+  EpiParams ep;
+  ep.kind = e->kind;
+  ep.n_rows = n_rows;
+  ep.batch = batch;
+  ep.ssq_in = e->ssq_in;
+  ep.ssq_parts = e->ssq_parts;
+  ep.ssq_ld = e->ssq_ld;
+  ep.ssq_inv_hidden = e->hidden > 0 ? 1.f / static_cast<float>(e->hidden) : 0.f;
+  ep.ssq_eps = e->ssq_eps;
+  ep.out = e->out;
+  ep.ld_out = e->ld_out;
+  ep.out_f32 = e->out_f32;
+  ep.relu = e->relu;
+  ep.bias = static_cast<const __half*>(e->bias);
+  ep.resid = e->resid;
+  ep.ld_resid = e->ld_resid;
+  ep.norm_w = static_cast<const __half*>(e->norm_w);
+  ep.xw = static_cast<__half*>(e->xw);
+  ep.ld_xw = e->ld_xw;
+  ep.ssq_out = e->ssq_out;
+  ep.ssq_out_ld = e->ssq_out_ld;
+  ep.q_heads = e->q_heads;
+  ep.kv_heads = e->kv_heads;
+  ep.positions = e->positions;
+  ep.inv_freq = e->inv_freq;
+  ep.k_cache = static_cast<__half*>(e->k_cache);
+  ep.v_cache = static_cast<__half*>(e->v_cache);
+  ep.max_seq = e->max_seq;
+  ep.cache_batch_stride = e->kv_heads * e->max_seq * 128;
+  ep.q_norm_w = static_cast<const __half*>(e->q_norm_w);
+  ep.k_norm_w = static_cast<const __half*>(e->k_norm_w);
+  ep.qk_eps = e->qk_eps;
+  ep.am_val = e->am_val;
+  ep.am_idx = e->am_idx;
+  ep.am_ld = e->am_ld;
+  NPU_REQUIRE(ep.ssq_in == nullptr || e->hidden > 0, "projection: RMSNorm input needs hidden");
+  return proj_run(d_w, w_packed != 0, d_x, n_rows, k, batch, ep, d_workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), false);
 }

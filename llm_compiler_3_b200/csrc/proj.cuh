@@ -64,10 +64,23 @@ struct EpiParams {
   int am_ld = 0;
 };
 
-// Runs the projection.  w [n_rows, k] FP16 row-major, x [batch, k] FP16 row-major.
+// Runs the projection.  w is [n_rows, k] FP16 row-major, or (w_packed) the
+// panel layout pack_weight() writes; x [batch, k] FP16 row-major.
 // Workspace: proj_workspace_bytes(); zero-filled once, left zero-filled.
-int proj_run(const void* w, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
-             void* workspace, size_t workspace_bytes, cudaStream_t stream, bool pdl);
+int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int batch,
+             const EpiParams& ep, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+             bool pdl);
 size_t proj_workspace_bytes(int n_rows, int k, int batch);
+
+// Weight panels: 16 KB blocks [ceil(n/128)][k/64] of 128 rows x 64 columns,
+// each already in the 128-byte-swizzled K-major layout the tensor cores read,
+// so one contiguous bulk copy moves a block from HBM to shared memory.
+size_t packed_weight_bytes(int n_rows, int k);
+// Packs n_src_rows source rows (row pitch src_pitch elements) into a panel
+// buffer of dst_rows rows.  row_mode 0: destination row = row_offset + i;
+// row_mode 1: rows interleave per 64 into 128-row tiles, [gate 64 | up 64]:
+// destination row = (i / 64) * 128 + i % 64 + row_offset (row_offset 0 or 64).
+int pack_weight(const void* src, size_t src_pitch, int n_src_rows, int k, void* dst, int dst_rows,
+                int row_mode, int row_offset, cudaStream_t stream);
 
 }  // namespace npu_b200

@@ -352,10 +352,12 @@ int allocate(npu_b200_ctx* c) {
   const size_t cache_elems = B * c->kv_loc * P.max_seq * D;
   for (int l = 0; l < P.layers; ++l) {
     LayerBuffers& L = c->layers[l];
-    if ((rc = dalloc(c, (c->q_loc + 2 * c->kv_loc) * D * H, &L.w_qkv, false)) ||
-        (rc = dalloc(c, H * c->q_loc * D, &L.w_o, false)) ||
-        (rc = dalloc(c, 2 * static_cast<size_t>(c->ffn_loc) * H, &L.w_gu, false)) ||
-        (rc = dalloc(c, H * c->ffn_loc, &L.w_down, false)) ||
+    const int qkv_rows = (c->q_loc + 2 * c->kv_loc) * static_cast<int>(D);
+    if ((rc = dalloc(c, packed_weight_bytes(qkv_rows, static_cast<int>(H)) / 2, &L.w_qkv)) ||
+        (rc = dalloc(c, packed_weight_bytes(static_cast<int>(H), c->q_loc * static_cast<int>(D)) / 2,
+                     &L.w_o)) ||
+        (rc = dalloc(c, packed_weight_bytes(2 * c->ffn_loc, static_cast<int>(H)) / 2, &L.w_gu)) ||
+        (rc = dalloc(c, packed_weight_bytes(static_cast<int>(H), c->ffn_loc) / 2, &L.w_down)) ||
         (rc = dalloc(c, H, &L.in_norm, false)) || (rc = dalloc(c, H, &L.post_norm, false)) ||
         (rc = dalloc(c, cache_elems, &L.k_cache)) || (rc = dalloc(c, cache_elems, &L.v_cache)))
       return rc;
@@ -366,7 +368,7 @@ int allocate(npu_b200_ctx* c) {
   if (P.vocab > 0) {
     if ((rc = dalloc(c, static_cast<size_t>(P.vocab) * H, &c->embed, false)) ||
         (rc = dalloc(c, H, &c->final_norm, false)) ||
-        (rc = dalloc(c, static_cast<size_t>(c->vocab_loc) * H, &c->lm_head, false)))
+        (rc = dalloc(c, packed_weight_bytes(c->vocab_loc, static_cast<int>(H)) / 2, &c->lm_head)))
       return rc;
     const int lm_tiles = (c->vocab_loc + 127) / 128;
     if ((rc = dalloc(c, static_cast<size_t>(lm_tiles) * B, &c->am_val)) ||
@@ -450,43 +452,73 @@ int place_weight(npu_b200_ctx* c, int layer, int kind, const void* src, size_t b
   int rc = 0;
   const uint8_t* s = static_cast<const uint8_t*>(src);
   cudaStream_t st = c->stream;
+  // The source may still be being written by work on other streams (e.g. the
+  // caller's generator kernels): the context stream does not order with them.
+  NPU_TRY_CUDA(cudaDeviceSynchronize());
+  // Matrices are packed into weight panels from a device copy of the source.
+  void* tmp = nullptr;
+  auto device_source = [&](const void** dsrc) -> int {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, src) == cudaSuccess &&
+        (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) &&
+        attr.device == c->device) {
+      *dsrc = src;
+      return NPU_B200_OK;
+    }
+    cudaGetLastError();
+    NPU_TRY_CUDA(cudaMalloc(&tmp, bytes));
+    // Stream-ordered with the packing kernel that reads it (a synchronous copy
+    // from pageable memory may return before its DMA has landed).
+    NPU_TRY_CUDA(cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyDefault, st));
+    *dsrc = tmp;
+    return NPU_B200_OK;
+  };
+  struct TmpGuard {
+    void** p;
+    ~TmpGuard() {
+      if (*p) cudaFree(*p);
+    }
+  } guard{&tmp};
+  const int Hi = static_cast<int>(H), Di = static_cast<int>(D);
   if (kind < kPerLayerKinds) {
     LayerBuffers& L = c->layers[layer];
+    const void* d = nullptr;
     switch (kind) {
       case kQ:
       case kK:
       case kV: {
         const int heads = kind == kQ ? P.heads : P.kv_heads;
         const int loc = kind == kQ ? c->q_loc : c->kv_loc;
-        if ((rc = expect(heads * D * H))) return rc;
-        const size_t row0 = kind == kQ ? 0 : (kind == kK ? c->q_loc : c->q_loc + c->kv_loc) * D;
-        NPU_TRY_CUDA(cudaMemcpyAsync(L.w_qkv + row0 * H, s + static_cast<size_t>(r) * loc * D * H * 2,
-                                     loc * D * H * 2, cudaMemcpyDefault, st));
+        if ((rc = expect(heads * D * H)) || (rc = device_source(&d))) return rc;
+        const int row0 = kind == kQ ? 0 : (kind == kK ? c->q_loc : c->q_loc + c->kv_loc) * Di;
+        const int rows = (c->q_loc + 2 * c->kv_loc) * Di;
+        if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(r) * loc * D * H,
+                              H, loc * Di, Hi, L.w_qkv, rows, 0, row0, st)))
+          return rc;
         break;
       }
       case kO: {  // [H, heads*D]: this rank's column block
-        if ((rc = expect(H * P.heads * D))) return rc;
-        const size_t cols = c->q_loc * D;
-        NPU_TRY_CUDA(cudaMemcpy2DAsync(L.w_o, cols * 2, s + static_cast<size_t>(r) * cols * 2,
-                                       P.heads * D * 2, cols * 2, H, cudaMemcpyDefault, st));
+        if ((rc = expect(H * P.heads * D)) || (rc = device_source(&d))) return rc;
+        const int cols = c->q_loc * Di;
+        if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(r) * cols,
+                              static_cast<size_t>(P.heads) * D, Hi, cols, L.w_o, Hi, 0, 0, st)))
+          return rc;
         break;
       }
       case kGate:
-      case kUp: {  // rows interleaved per 64: [gate 64 | up 64] blocks
-        if ((rc = expect(static_cast<size_t>(P.ffn) * H))) return rc;
-        const size_t blk = 64 * H * 2;
-        const uint8_t* base = s + static_cast<size_t>(r) * c->ffn_loc * H * 2;
-        uint8_t* dst = reinterpret_cast<uint8_t*>(L.w_gu) + (kind == kUp ? blk : 0);
-        NPU_TRY_CUDA(cudaMemcpy2DAsync(dst, 2 * blk, base, blk, blk, c->ffn_loc / 64,
-                                       cudaMemcpyDefault, st));
+      case kUp: {  // rows interleaved per 64 into [gate 64 | up 64] tiles
+        if ((rc = expect(static_cast<size_t>(P.ffn) * H)) || (rc = device_source(&d))) return rc;
+        if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(r) * c->ffn_loc * H,
+                              H, c->ffn_loc, Hi, L.w_gu, 2 * c->ffn_loc, 1, kind == kUp ? 64 : 0,
+                              st)))
+          return rc;
         break;
       }
       case kDown: {  // [H, ffn]: this rank's column block
-        if ((rc = expect(H * P.ffn))) return rc;
-        const size_t cols = c->ffn_loc;
-        NPU_TRY_CUDA(cudaMemcpy2DAsync(L.w_down, cols * 2, s + static_cast<size_t>(r) * cols * 2,
-                                       static_cast<size_t>(P.ffn) * 2, cols * 2, H,
-                                       cudaMemcpyDefault, st));
+        if ((rc = expect(H * P.ffn)) || (rc = device_source(&d))) return rc;
+        if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(r) * c->ffn_loc,
+                              static_cast<size_t>(P.ffn), Hi, c->ffn_loc, L.w_down, Hi, 0, 0, st)))
+          return rc;
         break;
       }
       case kInNorm:
@@ -516,10 +548,11 @@ int place_weight(npu_b200_ctx* c, int layer, int kind, const void* src, size_t b
       NPU_TRY_CUDA(cudaMemcpyAsync(c->final_norm, s, H * 2, cudaMemcpyDefault, st));
       c->have[top + 1] = 1;
     } else {
-      if ((rc = expect(static_cast<size_t>(P.vocab) * H))) return rc;
-      NPU_TRY_CUDA(cudaMemcpyAsync(c->lm_head, s + static_cast<size_t>(c->vocab_off) * H * 2,
-                                   static_cast<size_t>(c->vocab_loc) * H * 2, cudaMemcpyDefault,
-                                   st));
+      const void* d = nullptr;
+      if ((rc = expect(static_cast<size_t>(P.vocab) * H)) || (rc = device_source(&d))) return rc;
+      if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(c->vocab_off) * H, H,
+                            c->vocab_loc, Hi, c->lm_head, c->vocab_loc, 0, 0, st)))
+        return rc;
       c->have[top + 2] = 1;
     }
   }
@@ -579,13 +612,13 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
     e.ld_xw = P.hidden;
     e.ssq_out = c->ssq;
     e.ssq_out_ld = P.max_batch;
-    return proj_run(w, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
+    return proj_run(w, true, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
   }
   e.kind = kEpiStore;
   e.out = c->partial;
   e.ld_out = P.hidden;
   e.out_f32 = 1;
-  int rc = proj_run(w, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
+  int rc = proj_run(w, true, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
   if (rc) return rc;
   if ((rc = check_nccl(g_nccl.AllReduce(c->partial, c->partial,
                                         static_cast<size_t>(batch) * P.hidden, ncclFloat32,
@@ -647,7 +680,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     q.q_norm_w = L.q_norm;
     q.k_norm_w = L.k_norm;
     q.qk_eps = P.eps;
-    if ((rc = proj_run(L.w_qkv, c->xw, q.n_rows, H, batch, q, c->proj_ws, c->proj_ws_bytes, s,
+    if ((rc = proj_run(L.w_qkv, true, c->xw, q.n_rows, H, batch, q, c->proj_ws, c->proj_ws_bytes, s,
                        true)))
       return rc;
     if ((rc = flash_decode_run(c->q_buf, L.k_cache, L.v_cache, c->d_seq_lens, c->attn, batch,
@@ -662,7 +695,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     norm_input(c, &g);
     g.out = c->act;
     g.ld_out = c->ffn_loc;
-    if ((rc = proj_run(L.w_gu, c->xw, g.n_rows, H, batch, g, c->proj_ws, c->proj_ws_bytes, s,
+    if ((rc = proj_run(L.w_gu, true, c->xw, g.n_rows, H, batch, g, c->proj_ws, c->proj_ws_bytes, s,
                        true)))
       return rc;
     const __half* next = l + 1 < P.layers ? c->layers[l + 1].in_norm
@@ -680,7 +713,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
   a.am_val = c->am_val;
   a.am_idx = c->am_idx;
   a.am_ld = P.max_batch;
-  if ((rc = proj_run(c->lm_head, c->xw, c->vocab_loc, H, batch, a, c->proj_ws, c->proj_ws_bytes,
+  if ((rc = proj_run(c->lm_head, true, c->xw, c->vocab_loc, H, batch, a, c->proj_ws, c->proj_ws_bytes,
                      s, true)))
     return rc;
   const int lm_tiles = (c->vocab_loc + 127) / 128;

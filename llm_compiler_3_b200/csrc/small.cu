@@ -20,47 +20,47 @@ namespace {
 
 constexpr int kChunk = 128;
 
+// One CTA per (128-row chunk, token): every element is an independent load, so
+// the whole update is one memory round trip wide.
 __global__ void __launch_bounds__(kChunk)
     residual_update_kernel(ResidualUpdate p) {
+  pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[kChunk / 32];
   const int n = blockIdx.x * kChunk + threadIdx.x;
+  const int b = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float w = __half2float(p.norm_w[n]);
-  if (blockIdx.x == 0 && p.positions && p.seq_lens)
-    for (int b = threadIdx.x; b < p.batch; b += blockDim.x) p.seq_lens[b] = p.positions[b] + 1;
-  for (int b = 0; b < p.batch; ++b) {
-    float h;
-    if (p.mode == kResidFromEmbedding) {
-      const int tok = p.tokens[b];
-      if (tok < 0 || tok >= p.vocab) {
-        if (threadIdx.x == 0) report_error(kDevErrBounds);
-        h = 0.f;
-      } else {
-        h = __half2float(p.embed[static_cast<size_t>(tok) * p.hidden + n]);
-      }
-    } else if (p.mode == kResidFromHidden) {
-      h = __half2float(p.hidden_in[static_cast<size_t>(b) * p.hidden + n]);
+  if (blockIdx.x == 0 && b == 0 && p.positions && p.seq_lens)
+    for (int i = threadIdx.x; i < p.batch; i += blockDim.x) p.seq_lens[i] = p.positions[i] + 1;
+  float h;
+  if (p.mode == kResidFromEmbedding) {
+    const int tok = p.tokens[b];
+    if (tok < 0 || tok >= p.vocab) {
+      if (threadIdx.x == 0) report_error(kDevErrBounds);
+      h = 0.f;
     } else {
-      h = p.resid[static_cast<size_t>(b) * p.hidden + n] +
-          p.partial[static_cast<size_t>(b) * p.hidden + n];
+      h = __half2float(p.embed[static_cast<size_t>(tok) * p.hidden + n]);
     }
-    p.resid[static_cast<size_t>(b) * p.hidden + n] = h;
-    p.xw[static_cast<size_t>(b) * p.hidden + n] = __float2half_rn(h * w);
-    float s = h * h;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-#pragma unroll
-      for (int i = 0; i < kChunk / 32; ++i) t += red[i];
-      p.ssq_out[static_cast<size_t>(blockIdx.x) * p.ssq_ld + b] = t;
-    }
-    __syncthreads();
+  } else if (p.mode == kResidFromHidden) {
+    h = __half2float(p.hidden_in[static_cast<size_t>(b) * p.hidden + n]);
+  } else {
+    h = p.resid[static_cast<size_t>(b) * p.hidden + n] +
+        p.partial[static_cast<size_t>(b) * p.hidden + n];
   }
-  pdl_launch_dependents();
+  const float w = __half2float(p.norm_w[n]);
+  p.resid[static_cast<size_t>(b) * p.hidden + n] = h;
+  p.xw[static_cast<size_t>(b) * p.hidden + n] = __float2half_rn(h * w);
+  float s = h * h;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kChunk / 32; ++i) t += red[i];
+    p.ssq_out[static_cast<size_t>(blockIdx.x) * p.ssq_ld + b] = t;
+  }
 }
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(256)
     argmax_reduce_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
                          int n_tiles, int ld, int id_offset, float* __restrict__ out_val,
                          int32_t* __restrict__ out_idx) {
+  pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
   float bv = -INFINITY;
@@ -109,12 +110,12 @@ __global__ void __launch_bounds__(256)
     out_val[b] = bv;
     out_idx[b] = bi + id_offset;
   }
-  pdl_launch_dependents();
 }
 
 // gathered: [ranks][2][ld] as {values; ids} per rank.
 __global__ void argmax_combine_kernel(const float* __restrict__ gathered, int ranks, int ld,
                                       int batch, int32_t* __restrict__ out_ids) {
+  pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < batch) {
@@ -130,16 +131,15 @@ __global__ void argmax_combine_kernel(const float* __restrict__ gathered, int ra
     }
     out_ids[b] = bi;
   }
-  pdl_launch_dependents();
 }
 
 __global__ void store_hidden_kernel(const float* __restrict__ resid, __half* __restrict__ out,
                                     size_t count) {
+  pdl_launch_dependents();
   pdl_wait();
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     out[i] = __float2half_rn(resid[i]);
-  pdl_launch_dependents();
 }
 
 }  // namespace
@@ -148,7 +148,7 @@ int residual_update(const ResidualUpdate& p, cudaStream_t stream, bool pdl) {
   NPU_REQUIRE(p.hidden % kChunk == 0 && p.batch >= 1 && p.batch <= 1024,
               "residual update: hidden %d must be a multiple of 128", p.hidden);
   LaunchCfg cfg;
-  cfg.grid = dim3(p.hidden / kChunk);
+  cfg.grid = dim3(p.hidden / kChunk, p.batch);
   cfg.block = dim3(kChunk);
   cfg.stream = stream;
   cfg.pdl = pdl;

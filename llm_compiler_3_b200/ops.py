@@ -108,3 +108,29 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     _native.check(lib.npu_b200_linear(_ptr(x), _ptr(weight), _ptr(bias), _ptr(out), batch,
                                       n_rows, k, flags, _ptr(ws), ws.numel(), _stream()))
     return out
+
+
+def pack_weight(weight: torch.Tensor) -> torch.Tensor:
+    """Weight panels of weight [N, K] (see npu_b200_pack_weight): a flat uint8
+    tensor of 16 KB blocks streamed by one bulk copy each."""
+    _require(weight, "weight", ndim=2)
+    n, k = weight.shape
+    lib = _native.lib()
+    out = torch.empty(lib.npu_b200_packed_weight_bytes(n, k), dtype=torch.uint8,
+                      device=weight.device)
+    _native.check(lib.npu_b200_pack_weight(_ptr(weight), n, k, _ptr(out), _stream()))
+    return out
+
+
+def projection(x: torch.Tensor, weight: torch.Tensor, n_rows: int, epilogue,
+               packed: bool = False) -> None:
+    """Run npu_b200_projection with a filled _native.Epilogue (pointers set by the
+    caller).  x [B, K] FP16; weight [n_rows, K] FP16 or its packed panels."""
+    _require(x, "x", ndim=2)
+    batch, k = x.shape
+    lib = _native.lib()
+    need = lib.npu_b200_linear_workspace_size(n_rows, k, batch)
+    ws = workspace(need, x.device, slot=1)
+    _native.check(lib.npu_b200_projection(_ptr(x), _ptr(weight), 1 if packed else 0, batch,
+                                          n_rows, k, ctypes.byref(epilogue), _ptr(ws),
+                                          ws.numel(), _stream()))

@@ -51,5 +51,5 @@ def test_flash_decode_workspace_sizes():
     # One split needs no workspace; more splits need counters + partials.
     assert lib.npu_b200_flash_decode_workspace_size(64, 8, 128, 4096, 1) == 0
     size = lib.npu_b200_flash_decode_workspace_size(1, 8, 128, 4096, 16)
-    assert size == 256 + 8 * 16 * (8 * 128 + 16) * 4
+    assert size == 16384 * 4 + 8 * 16 * (8 * 128 + 16) * 4
     assert lib.npu_b200_flash_decode_workspace_size(1, 8, 128, 4096, 0) > 0
