@@ -44,6 +44,7 @@ struct LaunchCfg {
   size_t smem = 0;
   cudaStream_t stream = nullptr;
   bool pdl = false;
+  int cluster = 1;  // thread-block cluster size along x (1 = no cluster)
 };
 
 template <typename... KArgs, typename... Args>
@@ -53,13 +54,22 @@ int launch(const LaunchCfg& c, void (*kernel)(KArgs...), Args&&... args) {
   cfg.blockDim = c.block;
   cfg.dynamicSmemBytes = c.smem;
   cfg.stream = c.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
   if (c.pdl) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
   }
+  if (c.cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = c.cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = n ? attr : nullptr;
+  cfg.numAttrs = n;
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...),
                     "cudaLaunchKernelEx");
 }

@@ -49,7 +49,7 @@ struct ProjShape {
   static constexpr int kPitch = 128 + 4;        // floats per token column of the epilogue tile
   static constexpr int kTileBytes = kPitch * kChunkCols * 4;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kMiscBytes = 512 + 8 * BN;  // barriers, TMEM slot, per-token scalars
+  static constexpr int kMiscBytes = 640 + 8 * BN;  // barriers, TMEM slot, per-token scalars
 };
 
 __device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
@@ -84,13 +84,15 @@ __device__ __forceinline__ int owner_cta(long long i, long long total, int grid)
 }
 
 // Epilogue of one 16-token chunk of a finished 128-row tile.  Thread r holds
-// row tile*128 + r for tokens b0 .. b0+15 in v[].  All branches depend only on
-// the tile and the chunk, so every epilogue thread reaches the same barriers.
+// row tile*128 + r for tokens b0 .. b0+15 in v[]; tokens at or past col_end
+// are skipped.  All branches depend only on the tile and the chunk, so every
+// epilogue thread reaches the same barriers.
 __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile, int r, int b0,
                                                    float (&v)[kChunkCols], const float* rn,
-                                                   float* tile_s, float* aux, const int* pos_s) {
+                                                   float* tile_s, float* aux, const int* pos_s,
+                                                   int col_end) {
   constexpr int P = 128 + 4;
-  const int batch = ep.batch;
+  const int batch = col_end;  // tokens b0 + q < col_end of this chunk are written
 #pragma unroll
   for (int q = 0; q < kChunkCols; ++q) v[q] *= rn[b0 + q];
 
@@ -249,7 +251,7 @@ template <int BN>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ EpiParams ep, const uint8_t* __restrict__ w_packed,
-                int n_tiles, int kblocks, int stages, float* __restrict__ slots,
+                int n_tiles, int kblocks, int stages, int clustered, float* __restrict__ slots,
                 uint32_t* __restrict__ counters) {
   using S = ProjShape<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -261,16 +263,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  float* rn = reinterpret_cast<float*>(tmem_slot + 4);  // [BN] input RMSNorm scale per token
-  int* pos_s = reinterpret_cast<int*>(rn + BN);         // [BN] token positions (QKV)
-  float* aux = reinterpret_cast<float*>(pos_s + BN);    // [16] per-token scratch of a chunk
+  // Per-token scalars, padded by one chunk so a chunk starting anywhere below
+  // BN may read 16 entries.
+  float* rn = reinterpret_cast<float*>(tmem_slot + 4);          // [BN+16] RMSNorm scale
+  int* pos_s = reinterpret_cast<int*>(rn + BN + kChunkCols);    // [BN+16] token positions
+  float* aux = reinterpret_cast<float*>(pos_s + BN + kChunkCols);  // [16] chunk scratch
   volatile int* flags = reinterpret_cast<volatile int*>(aux + kChunkCols);  // abort, last
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(n_tiles) * kblocks;
   const int grid = gridDim.x, cta = blockIdx.x;
-  const long long it_begin = static_cast<long long>(cta) * total / grid;
-  const long long it_end = static_cast<long long>(cta + 1) * total / grid;
+  // Work split.  Stream-K: CTA c takes iterations [c*T/G, (c+1)*T/G) of the
+  // (tile, k-block) space.  Clustered split-K: the s CTAs of a cluster share
+  // one tile, member j taking k-blocks [j*KB/s, (j+1)*KB/s).
+  long long it_begin, it_end;
+  uint32_t crank = 0, csize = 1;
+  if (clustered) {
+    crank = cluster_ctarank();
+    csize = cluster_nctarank();
+    const long long tile = cta / static_cast<int>(csize);
+    it_begin = tile * kblocks + static_cast<long long>(crank) * kblocks / csize;
+    it_end = tile * kblocks + static_cast<long long>(crank + 1) * kblocks / csize;
+  } else {
+    it_begin = static_cast<long long>(cta) * total / grid;
+    it_end = static_cast<long long>(cta + 1) * total / grid;
+  }
 
   // The next kernel may be scheduled as soon as every CTA of this one is
   // resident; it waits for this grid's results itself (griddepcontrol.wait).
@@ -395,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     // ---------------- epilogue (tile row r = TMEM lane r) ----------------
     const int r = threadIdx.x;
     pdl_wait();
-    if (r < BN) {
+    if (r < BN + kChunkCols) {
       float scale = 1.f;
       if (ep.ssq_in != nullptr && r < ep.batch) {
         float s = 0.f;
@@ -408,6 +425,28 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     epi_sync();
     long long it = it_begin;
     int seg = 0;
+    if (clustered) {
+      // One segment: publish the FP32 partial in this CTA's own shared memory
+      // (the pipeline stages are idle once every MMA has completed).
+      const bool bad = flags[0] || !mbar_wait(&tfull[0], 0, kDevErrMmaTimeout);
+      if (epi_sync_or(bad)) {
+        flags[0] = 1;
+      } else {
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+        float* red = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
+          uint32_t rr[16];
+          tmem_ld16(taddr + c0, rr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < kChunkCols; ++q) red[(c0 + q) * S::kPitch + r] = __uint_as_float(rr[q]);
+        }
+        tc_fence_before();
+      }
+      it = it_end;  // skip the stream-K loop
+    }
     while (it < it_end) {
       const int tile = static_cast<int>(it / kblocks);
       const int kb0 = static_cast<int>(it % kblocks);
@@ -430,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           float v[kChunkCols];
 #pragma unroll
           for (int q = 0; q < kChunkCols; ++q) v[q] = __uint_as_float(rr[q]);
-          run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s);
+          run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
@@ -470,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
               for (int q = 0; q < kChunkCols; ++q) v[q] += __ldcg(other + q * 128);
             }
-            run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s);
+            run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
           }
           if (r == 0) counters[tile] = 0u;  // leave the workspace reusable
         }
@@ -481,6 +520,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
   }
 
+  if (clustered) {
+    // Cross-CTA reduction through distributed shared memory: member j sums the
+    // partials of every member, in rank order, for its share of the tokens and
+    // runs the epilogue on them.
+    cluster_sync_all();
+    if (warp < 4) {
+      const int r = threadIdx.x;
+      const int tile = cta / static_cast<int>(csize);
+      const int c_begin = static_cast<int>(static_cast<long long>(crank) * ep.batch / csize);
+      const int c_end = static_cast<int>(static_cast<long long>(crank + 1) * ep.batch / csize);
+      const uint32_t red0 = smem_u32(smem);
+      const bool ok = !epi_sync_or(flags[0] != 0);
+      for (int b0 = c_begin; ok && b0 < c_end; b0 += kChunkCols) {
+        float v[kChunkCols];
+#pragma unroll
+        for (int q = 0; q < kChunkCols; ++q) v[q] = 0.f;
+        for (uint32_t m = 0; m < csize; ++m) {
+          const uint32_t base = cluster_map(red0, m);
+#pragma unroll
+          for (int q = 0; q < kChunkCols; ++q)
+            if (b0 + q < c_end) v[q] += ld_cluster_f32(base + ((b0 + q) * S::kPitch + r) * 4);
+        }
+        run_epilogue_chunk(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
+      }
+    }
+    cluster_sync_all();  // no CTA leaves while a peer may still read its partial
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {
@@ -506,11 +572,18 @@ size_t smem_for(int stages) {
 
 int bn_for(int batch) { return batch <= 16 ? 16 : batch <= 32 ? 32 : batch <= 64 ? 64 : 128; }
 
+constexpr int kMaxCluster = 8;  // portable thread-block cluster size
+
 struct Geometry {
   int bn, n_tiles, kblocks, grid;
+  int split;       // > 0: clustered split-K with `split` CTAs per tile; 0: stream-K
   size_t counter_bytes, slot_bytes;
 };
 
+// Few tiles (fewer than one per CTA slot): split each tile's K over a cluster
+// and reduce through distributed shared memory -- no global scratch, no
+// serialized fix-up.  Many tiles: stream-K over every CTA slot, where a tile
+// has at most a couple of contributors.
 Geometry geometry(int n_rows, int k, int batch) {
   Geometry g;
   g.bn = bn_for(batch);
@@ -518,6 +591,17 @@ Geometry geometry(int n_rows, int k, int batch) {
   g.kblocks = k / 64;
   const long long total = static_cast<long long>(g.n_tiles) * g.kblocks;
   const long long slots_total = static_cast<long long>(sm_count()) * kCtasPerSm;
+  g.split = 0;
+  if (2ll * g.n_tiles <= slots_total) {
+    int best = 1;
+    for (int s = 1; s <= kMaxCluster && g.kblocks / s >= 2; ++s)
+      if (static_cast<long long>(g.n_tiles) * s <= slots_total) best = s;
+    g.split = best;
+    g.grid = g.n_tiles * best;
+    g.counter_bytes = 0;
+    g.slot_bytes = 0;
+    return g;
+  }
   g.grid = static_cast<int>(total < slots_total ? total : slots_total);
   g.counter_bytes = kCounterBytes;
   g.slot_bytes = static_cast<size_t>(g.n_tiles + g.grid - 1) * 128 * g.bn * 4;
@@ -539,7 +623,9 @@ int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& e
   cfg.smem = smem;
   cfg.stream = stream;
   cfg.pdl = pdl;
-  return launch(cfg, kern, wm, xm, ep, w_packed, g.n_tiles, g.kblocks, stages, slots, counters);
+  cfg.cluster = g.split > 1 ? g.split : 1;
+  return launch(cfg, kern, wm, xm, ep, w_packed, g.n_tiles, g.kblocks, stages,
+                g.split > 0 ? 1 : 0, slots, counters);
 }
 
 // One thread per 16-byte chunk of the source: row i, chunk c (elements 8c..8c+7)
@@ -627,9 +713,9 @@ int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int
 
   const Geometry g = geometry(n_rows, k, batch);
   const size_t need = g.counter_bytes + g.slot_bytes;
-  NPU_REQUIRE(workspace && workspace_bytes >= need,
+  NPU_REQUIRE(need == 0 || (workspace && workspace_bytes >= need),
               "projection: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-  NPU_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+  NPU_REQUIRE(need == 0 || (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
               "projection: workspace must be 256-byte aligned");
   CUtensorMap wm, xm;
   int rc = 0;
@@ -638,8 +724,9 @@ int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int
   else if ((rc = make_tensor_map_2d(&wm, w, n_rows, k, 128, 64)))
     return rc;
   if ((rc = make_tensor_map_2d(&xm, x, batch, k, g.bn, 64))) return rc;
-  uint32_t* counters = static_cast<uint32_t*>(workspace);
-  float* slots = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.counter_bytes);
+  uint32_t* counters = need ? static_cast<uint32_t*>(workspace) : nullptr;
+  float* slots =
+      need ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.counter_bytes) : nullptr;
   const uint8_t* wp = w_packed ? static_cast<const uint8_t*>(w) : nullptr;
   switch (g.bn) {
     case 16: return launch_proj<16>(wm, xm, ep, wp, g, slots, counters, stream, pdl);

@@ -207,11 +207,27 @@ def test_stack_argmax_two_layers(cuda):
         lambda i: per_layer[i], layers, top["model.embed_tokens.weight"], top["model.norm.weight"],
         top["lm_head.weight"], tokens, positions,
         lambda i: (caches[i][0].clone(), caches[i][1].clone()), shape, return_logits=True)
-    mism = np.nonzero(ids != ref_ids.numpy())[0]
-    if len(mism):
-        top2 = logits[mism].topk(2, dim=-1).values
-        gaps = (top2[:, 0] - top2[:, 1]).tolist()
-        pytest.fail(f"{len(mism)} of {batch} ids differ at {mism.tolist()}; oracle top-2 gaps {gaps}")
+    _check_ids(ids, ref_ids, logits)
+
+
+def _check_ids(ids, ref_ids, logits):
+    """Greedy ids must equal the oracle's wherever the oracle's top-2 logit gap
+    exceeds the error the FP16 intermediates can cause (about 1e-3 of the logit
+    scale here: every projection input is an FP16 tensor); closer pairs are
+    near-ties, reported with their gap, and may only differ by picking the
+    runner-up."""
+    ids = np.asarray(ids)
+    ref = ref_ids.numpy()
+    top2 = logits.topk(2, dim=-1)
+    gaps = (top2.values[:, 0] - top2.values[:, 1]).numpy()
+    tie_bound = 4e-3 * float(logits.std())
+    mism = np.nonzero(ids != ref)[0]
+    for b in mism:
+        assert gaps[b] < tie_bound, (
+            f"sequence {b}: id {ids[b]} != oracle {ref[b]} with top-2 gap {gaps[b]:.3e} "
+            f">= bound {tie_bound:.3e}")
+        assert ids[b] == int(top2.indices[b, 1]), f"sequence {b}: not the oracle's runner-up"
+    assert len(mism) <= max(1, len(ids) // 16), f"{len(mism)} near-tie flips of {len(ids)}"
 
 
 def test_decode_errors_are_status_codes(cuda):

@@ -32,10 +32,13 @@ def test_grid_values_bit_exact(cuda, batch, n, k):
 
 
 @pytest.mark.parametrize("batch", [1, 2, 16, 17, 64, 100])
-@pytest.mark.parametrize("n,k", [(4096, 4096), (1024, 4096), (4096, 14336), (640, 1792)])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (1024, 4096), (4096, 14336), (640, 1792),
+                                 (20480, 4096), (28672, 512)])
 def test_random_fp32_out(cuda, batch, n, k):
     """Decode projection shapes (q/o 4096x4096, k/v 1024x4096, down 4096x14336, a
-    TP-8 shard) with outputs kept in FP32: stream-K splits of K across CTAs."""
+    TP-8 shard) with outputs kept in FP32.  Few tiles take the clustered split-K
+    path (reduction in distributed shared memory); 160+ tiles take stream-K
+    (partials through the workspace, last contributor finishes)."""
     from llm_compiler_3_b200 import _native, ops
     x = seeded((batch, k), 100 + batch)
     w = seeded((n, k), 200 + n, std=0.02)
