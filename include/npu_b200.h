@@ -99,6 +99,30 @@ NPU_B200_API int npu_b200_flash_decode(const void* d_q, const void* d_k, const v
                           int kv_heads, int head_dim, int max_seq, float scale, int num_splits,
                           void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* npu_b200_flash_decode without any device allocation (no counterpart in the
+ * reference: its compiled programs run on a simulator that owns all memory).
+ *
+ * For callers that cannot allocate device memory when they call attention:
+ * code running inside a host application that has already handed all HBM to its
+ * own pool allocator, code on a latency-critical path where the device-wide
+ * synchronization of cudaMalloc/cudaFree is unacceptable, or plugins whose host
+ * forbids device allocation after start-up.  The split-merge scratch is instead
+ * a fixed 4 MiB array in this library's device memory, present on every GPU that
+ * loads the library until the process exits.  A shape whose scratch would exceed
+ * 4 MiB (batch x kv_heads x splits x (8 x head_dim + 16) x 4 bytes plus 64 KiB of
+ * counters) is rejected with NPU_B200_E_INVALID.
+ *
+ * The first call on each device looks up the array's device address (with that
+ * device current), so make the first call before any stream capture.  Every call
+ * uses the same array and clears the counters it needs before its kernel runs;
+ * calls that overlap on the GPU (different streams, or concurrent graphs) race on
+ * the array.  Arguments and results are those of npu_b200_flash_decode. */
+NPU_B200_API int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, const void* d_v,
+                                               const int32_t* d_seq_lens, void* d_out, int batch,
+                                               int q_heads, int kv_heads, int head_dim,
+                                               int max_seq, float scale, int num_splits,
+                                               void* stream);
+
 /* Linear layer on tcgen05 tensor cores:
  *   out[b, n] = act( sum_k x[b, k] * w[n, k] + bias[n] ),  FP32 accumulation.
  *

@@ -18,6 +18,8 @@
 // (sequence, KV head)), so one launch produces the final FP16 output.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "host.hpp"
 
@@ -521,4 +523,67 @@ extern "C" int npu_b200_flash_decode(const void* d_q, const void* d_k, const voi
   return npu_b200::flash_decode_run(d_q, d_k, d_v, d_seq_lens, d_out, batch, q_heads, kv_heads,
                                     head_dim, max_seq, scale, num_splits, d_workspace,
                                     workspace_bytes, static_cast<cudaStream_t>(stream), false);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the split-merge scratch (counters + partial O, m, l)
+// lives in a fixed array in the module's device memory instead of a caller
+// buffer.  Every GPU that loads this library keeps this array until the
+// process exits.
+// ---------------------------------------------------------------------------
+namespace npu_b200 {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB per device
+static __device__ __align__(256) uint8_t g_flash_decode_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// The array's name is only a host-side stand-in for the symbol; the device
+// address differs per device and is looked up once, with that device current.
+int scratch_address(void** out) {
+  int dev = 0;
+  NPU_TRY_CUDA(cudaGetDevice(&dev));
+  NPU_REQUIRE(dev >= 0 && dev < kMaxDevices, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    NPU_TRY_CUDA(cudaGetSymbolAddress(&p, g_flash_decode_scratch));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return NPU_B200_OK;
+}
+
+}  // namespace
+}  // namespace npu_b200
+
+extern "C" int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, const void* d_v,
+                                             const int32_t* d_seq_lens, void* d_out, int batch,
+                                             int q_heads, int kv_heads, int head_dim, int max_seq,
+                                             float scale, int num_splits, void* stream) {
+  using namespace npu_b200;
+  clear_error();
+  NPU_REQUIRE(batch >= 1 && kv_heads >= 1 && max_seq >= 1 && num_splits >= 0 &&
+                  num_splits <= kMaxSplits && (head_dim == 64 || head_dim == 128),
+              "flash_decode_noalloc: invalid shape");
+  const size_t need = flash_decode_workspace(batch, kv_heads, head_dim, max_seq, num_splits);
+  NPU_REQUIRE(need <= kNoAllocScratchBytes,
+              "flash_decode_noalloc: this shape needs %zu bytes of split scratch, more than the "
+              "%zu-byte static scratch; use fewer splits or npu_b200_flash_decode",
+              need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (need > 0) {
+    // The array keeps whatever the previous call left: the split counters
+    // must start at zero.
+    const size_t units = static_cast<size_t>(batch) * kv_heads;
+    NPU_TRY_CUDA(cudaMemsetAsync(scratch, 0, units * sizeof(uint32_t), s));
+  }
+  return flash_decode_run(d_q, d_k, d_v, d_seq_lens, d_out, batch, q_heads, kv_heads, head_dim,
+                          max_seq, scale, num_splits, scratch, kNoAllocScratchBytes, s, false);
 }
