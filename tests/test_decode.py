@@ -245,3 +245,59 @@ def test_decode_errors_are_status_codes(cuda):
             dec.forward_hidden(torch.zeros(3, 4096, dtype=torch.float16), [1, 2, 3])
         with pytest.raises(_native.NpuError, match="no vocabulary"):
             dec.step([1], [0])
+
+
+def test_stack_config_full_size(cuda):
+    """The stack config at full size: 32 Llama-3-8B-shaped layers, LM head
+    4096x128256, batch 64, each sequence at position 4095 over a 4095-token cache.
+    Weights and caches are generated on the device (seeded) and read back layer by
+    layer for the oracle, so both sides see identical FP16 inputs."""
+    from llm_compiler_3_b200.plan import llama3_8b
+    from llm_compiler_3_b200.runtime import Decoder
+    shape = oracle.LLAMA3_8B
+    layers, batch, seq = 32, 64, 4096
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    H, D = shape.hidden, shape.head_dim
+    shapes = {"self_attn.q_proj.weight": (shape.heads * D, H),
+              "self_attn.k_proj.weight": (shape.kv_heads * D, H),
+              "self_attn.v_proj.weight": (shape.kv_heads * D, H),
+              "self_attn.o_proj.weight": (H, shape.heads * D),
+              "mlp.gate_proj.weight": (shape.ffn, H), "mlp.up_proj.weight": (shape.ffn, H),
+              "mlp.down_proj.weight": (H, shape.ffn)}
+
+    def randn(shp, seed, std):
+        gen.manual_seed(seed)
+        return (torch.randn(shp, device=dev, generator=gen) * std).half()
+
+    def layer(i):
+        w = {n: randn(s, 1000 + 16 * i + j, 0.02) for j, (n, s) in enumerate(shapes.items())}
+        w["input_layernorm.weight"] = torch.ones(H, dtype=torch.float16, device=dev)
+        w["post_attention_layernorm.weight"] = torch.ones(H, dtype=torch.float16, device=dev)
+        return w
+
+    embed = randn((shape.vocab, H), 11, 0.02)
+    lm = randn((shape.vocab, H), 12, 0.02)
+    norm = torch.ones(H, dtype=torch.float16, device=dev)
+    gen.manual_seed(7)
+    tokens = torch.randint(0, shape.vocab, (batch,), device=dev, generator=gen, dtype=torch.int32)
+    positions = torch.full((batch,), seq - 1, dtype=torch.int32)
+    with Decoder(llama3_8b(layers=layers, max_batch=batch, max_seq=seq)) as dec:
+        dec.set_weight("model.embed_tokens.weight", embed)
+        dec.set_weight("lm_head.weight", lm)
+        dec.set_weight("model.norm.weight", norm)
+        for i in range(layers):
+            for name, t in layer(i).items():
+                dec.set_weight(f"model.layers.{i}.{name}", t)
+            k, v = dec.kv_cache(i)
+            gen.manual_seed(50000 + 2 * i)
+            k[:, :, : seq - 1].normal_(generator=gen)
+            gen.manual_seed(50001 + 2 * i)
+            v[:, :, : seq - 1].normal_(generator=gen)
+        ids = dec.step(tokens.cpu().numpy(), positions.numpy())
+        torch.set_num_threads(os.cpu_count() or 1)
+        ref_ids, logits = oracle.stack_decode(
+            lambda i: {n: t.cpu() for n, t in layer(i).items()}, layers, embed.cpu(), norm.cpu(),
+            lm.cpu(), tokens.cpu(), positions,
+            lambda i: tuple(t.cpu() for t in dec.kv_cache(i)), shape, return_logits=True)
+    _check_ids(ids, ref_ids, logits)
