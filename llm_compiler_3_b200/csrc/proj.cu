@@ -83,6 +83,58 @@ __device__ __forceinline__ int owner_cta(long long i, long long total, int grid)
   return static_cast<int>(c);
 }
 
+// Column sums of a 16-token x 128-row chunk staged in tile_s ([q][r], pitch
+// 132): warp w reduces columns 4w..4w+3, each lane summing 4 rows before a
+// butterfly over the warp.  Lane 0 of each warp writes out[q].
+__device__ __forceinline__ void column_sums(const float* tile_s, float* out) {
+  constexpr int P = 128 + 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int q = warp * 4 + j;
+    const float* col = tile_s + q * P;
+    float s = col[lane] + col[lane + 32] + col[lane + 64] + col[lane + 96];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[q] = s;
+  }
+}
+
+// Column max / argmax (lowest row on ties) of the same staging, rows first_row + r.
+__device__ __forceinline__ void column_argmax(const float* tile_s, int first_row, float* out_val,
+                                              int* out_idx) {
+  constexpr int P = 128 + 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int q = warp * 4 + j;
+    const float* col = tile_s + q * P;
+    float bv = col[lane];
+    int bi = lane;
+#pragma unroll
+    for (int k = 1; k < 4; ++k) {
+      const float x = col[lane + 32 * k];
+      if (x > bv) {
+        bv = x;
+        bi = lane + 32 * k;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_val[q] = bv;
+      out_idx[q] = first_row + bi;
+    }
+  }
+}
+
 // Epilogue of one 16-token chunk of a finished 128-row tile.  Thread r holds
 // row tile*128 + r for tokens b0 .. b0+15 in v[]; tokens at or past col_end
 // are skipped.  All branches depend only on the tile and the chunk, so every
@@ -139,12 +191,10 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
       tile_s[q * P + r] = h2;
     }
     epi_sync();
-    if (r < kChunkCols && b0 + r < batch) {
-      float s = 0.f;
-#pragma unroll 8
-      for (int i = 0; i < 128; ++i) s += tile_s[r * P + i];
-      ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + b0 + r] = s;
-    }
+    column_sums(tile_s, aux);
+    epi_sync();
+    if (r < kChunkCols && b0 + r < batch)
+      ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + b0 + r] = aux[r];
     epi_sync();
   } else if (ep.kind == kEpiSwiGLU) {
 #pragma unroll
@@ -173,12 +223,9 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = v[q] * v[q];
       epi_sync();
-      if (r < kChunkCols) {
-        float s = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < 128; ++i) s += tile_s[r * P + i];
-        aux[r] = rsqrtf(s * (1.f / 128.f) + ep.qk_eps);
-      }
+      column_sums(tile_s, aux);
+      epi_sync();
+      if (r < kChunkCols) aux[r] = rsqrtf(aux[r] * (1.f / 128.f) + ep.qk_eps);
       epi_sync();
       const float wr = __half2float(nw[r]);
 #pragma unroll
@@ -193,9 +240,15 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
       for (int q = 0; q < kChunkCols; ++q) {
         if (b0 + q < batch) {
           const float partner = tile_s[q * P + (r ^ 64)];
-          const float theta = static_cast<float>(pos_s[b0 + q]) * f;
           float sn, cs;
-          sincosf(theta, &sn, &cs);
+          if (ep.rope_tab != nullptr) {  // cos / sin of this step's positions, precomputed
+            const float2 cssn =
+                reinterpret_cast<const float2*>(ep.rope_tab)[(b0 + q) * 64 + (r & 63)];
+            cs = cssn.x;
+            sn = cssn.y;
+          } else {
+            sincosf(static_cast<float>(pos_s[b0 + q]) * f, &sn, &cs);
+          }
           v[q] = r < 64 ? v[q] * cs - partner * sn : v[q] * cs + partner * sn;
         }
       }
@@ -230,18 +283,12 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
 #pragma unroll
     for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = valid ? v[q] : -INFINITY;
     epi_sync();
+    int* aux_i = reinterpret_cast<int*>(aux) + kChunkCols;
+    column_argmax(tile_s, tile * 128, aux, aux_i);
+    epi_sync();
     if (r < kChunkCols && b0 + r < batch) {
-      float best = -INFINITY;
-      int bi = tile * 128;
-      for (int i = 0; i < 128; ++i) {
-        const float x = tile_s[r * P + i];
-        if (x > best) {
-          best = x;
-          bi = tile * 128 + i;
-        }
-      }
-      ep.am_val[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = best;
-      ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = bi;
+      ep.am_val[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = aux[r];
+      ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = aux_i[r];
     }
     epi_sync();
   }
@@ -267,8 +314,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   // BN may read 16 entries.
   float* rn = reinterpret_cast<float*>(tmem_slot + 4);          // [BN+16] RMSNorm scale
   int* pos_s = reinterpret_cast<int*>(rn + BN + kChunkCols);    // [BN+16] token positions
-  float* aux = reinterpret_cast<float*>(pos_s + BN + kChunkCols);  // [16] chunk scratch
-  volatile int* flags = reinterpret_cast<volatile int*>(aux + kChunkCols);  // abort, last
+  float* aux = reinterpret_cast<float*>(pos_s + BN + kChunkCols);  // [32] chunk scratch
+  volatile int* flags = reinterpret_cast<volatile int*>(aux + 2 * kChunkCols);  // abort, last
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(n_tiles) * kblocks;
@@ -415,8 +462,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (r < BN + kChunkCols) {
       float scale = 1.f;
       if (ep.ssq_in != nullptr && r < ep.batch) {
+        // 16 independent loads per batch: one memory round trip per 16 parts.
         float s = 0.f;
-        for (int p = 0; p < ep.ssq_parts; ++p) s += ep.ssq_in[static_cast<size_t>(p) * ep.ssq_ld + r];
+        for (int p0 = 0; p0 < ep.ssq_parts; p0 += 16) {
+          float t[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            t[j] = p0 + j < ep.ssq_parts ? ep.ssq_in[static_cast<size_t>(p0 + j) * ep.ssq_ld + r] : 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) s += t[j];
+        }
         scale = rsqrtf(s * ep.ssq_inv_hidden + ep.ssq_eps);
       }
       rn[r] = scale;
@@ -504,10 +559,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             float v[kChunkCols];
 #pragma unroll
             for (int q = 0; q < kChunkCols; ++q) v[q] = 0.f;
-            for (int c = cf; c <= cl; ++c) {
-              const float* other = slots + static_cast<size_t>(tile + c) * 128 * BN + c0 * 128 + r;
+            // Loads of up to 4 contributors in flight together; sums in CTA order.
+            for (int c = cf; c <= cl; c += 4) {
+              float t[4][kChunkCols];
 #pragma unroll
-              for (int q = 0; q < kChunkCols; ++q) v[q] += __ldcg(other + q * 128);
+              for (int u = 0; u < 4; ++u) {
+                const float* other =
+                    slots + static_cast<size_t>(tile + c + u) * 128 * BN + c0 * 128 + r;
+#pragma unroll
+                for (int q = 0; q < kChunkCols; ++q)
+                  t[u][q] = c + u <= cl ? __ldcg(other + q * 128) : 0.f;
+              }
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int q = 0; q < kChunkCols; ++q) v[q] += t[u][q];
             }
             run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
           }
@@ -536,11 +602,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         float v[kChunkCols];
 #pragma unroll
         for (int q = 0; q < kChunkCols; ++q) v[q] = 0.f;
-        for (uint32_t m = 0; m < csize; ++m) {
-          const uint32_t base = cluster_map(red0, m);
+        // Loads of up to 4 members in flight together; sums in rank order.
+        for (uint32_t m = 0; m < csize; m += 4) {
+          float t[4][kChunkCols];
 #pragma unroll
-          for (int q = 0; q < kChunkCols; ++q)
-            if (b0 + q < c_end) v[q] += ld_cluster_f32(base + ((b0 + q) * S::kPitch + r) * 4);
+          for (int u = 0; u < 4; ++u) {
+            const bool member = m + u < csize;
+            const uint32_t base = cluster_map(red0, member ? m + u : 0);
+#pragma unroll
+            for (int q = 0; q < kChunkCols; ++q)
+              t[u][q] = (member && b0 + q < c_end)
+                            ? ld_cluster_f32(base + ((b0 + q) * S::kPitch + r) * 4)
+                            : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int q = 0; q < kChunkCols; ++q) v[q] += t[u][q];
         }
         run_epilogue_chunk(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
       }
@@ -574,6 +652,61 @@ int bn_for(int batch) { return batch <= 16 ? 16 : batch <= 32 ? 32 : batch <= 64
 
 constexpr int kMaxCluster = 8;  // portable thread-block cluster size
 
+template <int BN>
+int stages_for();
+template <int BN>
+size_t smem_for(int stages);
+
+// Stand-in with proj_kernel's launch shape (threads, CTAs per SM, dynamic
+// shared memory) for cluster-occupancy queries.  For proj_kernel itself the
+// occupancy API reports one CTA per SM, while the hardware co-schedules two
+// (measured: 32 clusters of 8 start together); the stand-in's answer matches
+// what is observed.
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) proj_shape_twin(int* never) {
+  if (never) never[threadIdx.x] = 0;
+}
+
+// How many clusters of `s` CTAs (with proj_kernel<BN>'s shape) can be
+// resident at once (cached; depends on how clusters pack into GPCs, not only
+// on the SM count).  Falls back to a conservative estimate without a device.
+template <int BN>
+int max_active_clusters(int s) {
+  static int cache[64][kMaxCluster + 1] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev][s] != 0) return cache[dev][s];
+  int n = 0;
+  const size_t smem = smem_for<BN>(stages_for<BN>());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(s * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = s;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  if (cudaFuncSetAttribute(proj_shape_twin, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n, proj_shape_twin, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = (sm_count() * kCtasPerSm * 3 / 5) / s;  // no device: leave ~40% slack for packing
+  }
+  cache[dev][s] = n;
+  return n;
+}
+
+int max_clusters(int bn, int s) {
+  switch (bn) {
+    case 16: return max_active_clusters<16>(s);
+    case 32: return max_active_clusters<32>(s);
+    case 64: return max_active_clusters<64>(s);
+    default: return max_active_clusters<128>(s);
+  }
+}
+
 struct Geometry {
   int bn, n_tiles, kblocks, grid;
   int split;       // > 0: clustered split-K with `split` CTAs per tile; 0: stream-K
@@ -582,8 +715,10 @@ struct Geometry {
 
 // Few tiles (fewer than one per CTA slot): split each tile's K over a cluster
 // and reduce through distributed shared memory -- no global scratch, no
-// serialized fix-up.  Many tiles: stream-K over every CTA slot, where a tile
-// has at most a couple of contributors.
+// serialized fix-up.  The cluster size is the largest for which every cluster
+// is resident at once: a second wave of clusters would double the time.
+// Many tiles: stream-K over every CTA slot, where a tile has at most a couple
+// of contributors.
 Geometry geometry(int n_rows, int k, int batch) {
   Geometry g;
   g.bn = bn_for(batch);
@@ -594,8 +729,8 @@ Geometry geometry(int n_rows, int k, int batch) {
   g.split = 0;
   if (2ll * g.n_tiles <= slots_total) {
     int best = 1;
-    for (int s = 1; s <= kMaxCluster && g.kblocks / s >= 2; ++s)
-      if (static_cast<long long>(g.n_tiles) * s <= slots_total) best = s;
+    for (int s = 2; s <= kMaxCluster && g.kblocks / s >= 2; ++s)
+      if (g.n_tiles <= max_clusters(g.bn, s)) best = s;
     g.split = best;
     g.grid = g.n_tiles * best;
     g.counter_bytes = 0;

@@ -50,6 +50,7 @@ struct EpiParams {
   int q_heads = 0, kv_heads = 0;
   const int32_t* positions = nullptr;
   const float* inv_freq = nullptr;  // [64]
+  const float* rope_tab = nullptr;  // optional [batch][64] (cos, sin) of positions x inv_freq
   __half* k_cache = nullptr;        // [batch_cap][kv_heads][max_seq][128]
   __half* v_cache = nullptr;
   int max_seq = 0;

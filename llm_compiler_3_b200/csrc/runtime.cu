@@ -276,6 +276,7 @@ struct npu_b200_ctx {
   std::vector<LayerBuffers> layers;
   __half *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
   float *resid = nullptr, *ssq = nullptr, *partial = nullptr, *d_inv_freq = nullptr;
+  float* rope_tab = nullptr;  // [max_batch][64] (cos, sin) of this step's positions
   __half *xw = nullptr, *q_buf = nullptr, *attn = nullptr, *act = nullptr, *hidden_io = nullptr;
   int32_t *d_tokens = nullptr, *d_positions = nullptr, *d_seq_lens = nullptr, *d_ids = nullptr;
   float *am_val = nullptr, *gather_send = nullptr, *gather_recv = nullptr;
@@ -383,7 +384,8 @@ int allocate(npu_b200_ctx* c) {
       (rc = dalloc(c, B * c->ffn_loc, &c->act)) || (rc = dalloc(c, B * H, &c->hidden_io)) ||
       (rc = dalloc(c, B, &c->d_tokens)) || (rc = dalloc(c, B, &c->d_positions)) ||
       (rc = dalloc(c, B, &c->d_seq_lens)) || (rc = dalloc(c, B, &c->d_ids)) ||
-      (rc = dalloc(c, P.inv_freq.size(), &c->d_inv_freq)))
+      (rc = dalloc(c, P.inv_freq.size(), &c->d_inv_freq)) ||
+      (rc = dalloc(c, B * 128, &c->rope_tab)))
     return rc;
   NPU_TRY_CUDA(cudaMemcpy(c->d_inv_freq, P.inv_freq.data(), P.inv_freq.size() * sizeof(float),
                           cudaMemcpyHostToDevice));
@@ -658,6 +660,8 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     u.ssq_ld = P.max_batch;
     u.positions = c->d_positions;
     u.seq_lens = c->d_seq_lens;
+    u.inv_freq = c->d_inv_freq;
+    u.rope_tab = c->rope_tab;
     if ((rc = residual_update(u, s, true))) return rc;
   }
   for (int l = 0; l < P.layers; ++l) {
@@ -673,6 +677,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     q.kv_heads = c->kv_loc;
     q.positions = c->d_positions;
     q.inv_freq = c->d_inv_freq;
+    q.rope_tab = c->rope_tab;
     q.k_cache = L.k_cache;
     q.v_cache = L.v_cache;
     q.max_seq = P.max_seq;

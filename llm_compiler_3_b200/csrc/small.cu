@@ -32,6 +32,13 @@ __global__ void __launch_bounds__(kChunk)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (blockIdx.x == 0 && b == 0 && p.positions && p.seq_lens)
     for (int i = threadIdx.x; i < p.batch; i += blockDim.x) p.seq_lens[i] = p.positions[i] + 1;
+  // This step's RoPE angles, once for every layer: theta = float(pos) * inv_freq
+  // in FP32 (as transformers forms them), then an accurate sincos.
+  if (blockIdx.x == 0 && p.rope_tab && p.positions && threadIdx.x < 64) {
+    float sn, cs;
+    sincosf(static_cast<float>(p.positions[b]) * p.inv_freq[threadIdx.x], &sn, &cs);
+    reinterpret_cast<float2*>(p.rope_tab)[b * 64 + threadIdx.x] = make_float2(cs, sn);
+  }
   float h;
   if (p.mode == kResidFromEmbedding) {
     const int tok = p.tokens[b];

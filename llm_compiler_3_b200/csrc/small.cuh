@@ -29,6 +29,8 @@ struct ResidualUpdate {
   int ssq_ld = 0;
   const int32_t* positions = nullptr; // optional: seq_lens[b] = positions[b] + 1
   int32_t* seq_lens = nullptr;
+  const float* inv_freq = nullptr;    // optional with rope_tab: [64] RoPE inverse frequencies
+  float* rope_tab = nullptr;          // [batch][64] (cos, sin) of positions[b] * inv_freq[i]
 };
 
 int residual_update(const ResidualUpdate& p, cudaStream_t stream, bool pdl);
