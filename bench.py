@@ -334,6 +334,21 @@ def run_b200(a):
     wall = time.perf_counter() - t0
     e2e_elapsed = max_over_ranks(max(s2.elapsed_time(e2) / 1e3, wall))
 
+    # The north-star case: the same stack and cache at batch 1 (one sequence,
+    # position 4095), through its own captured graph in the same context.
+    tok1, pos1, ids1 = tokens[:1].clone(), positions[:1].clone(), ids[:1].clone()
+    for _ in range(a.warmup):
+        dec.step_device(tok1, pos1, ids1)
+    barrier()
+    torch.cuda.synchronize()
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s1.record(stream)
+    for _ in range(a.steps):
+        dec.step_device(tok1, pos1, ids1)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    b1_elapsed = max_over_ranks(s1.elapsed_time(e1) / 1e3)
+
     # Dominant kernel (flash-decoding: ~70% of the step's bytes), timed alone on
     # this rank's shard shape with CUDA events around graph replays that
     # alternate between two layers' caches.
@@ -392,6 +407,11 @@ def run_b200(a):
                           "frac": sb / t_step / 1e9 / (peak * world), "peak_GBps": peak * world},
         "e2e": {"value": a.batch * a.steps / e2e_elapsed, "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * 4 * a.batch, "d2h_bytes_per_step": 4 * a.batch},
+        "batch1_stack": {
+            "tokens_per_s": a.steps / b1_elapsed, "ms_per_token": b1_elapsed / a.steps * 1e3,
+            "algorithmic_bytes": step_bytes(1, a.layers, a.seq),
+            "step_roofline_frac": step_bytes(1, a.layers, a.seq) / (b1_elapsed / a.steps) / 1e9
+            / (peak * world)},
         "gpu_launches": per_step_launches * a.steps,
         "device_error_bits": status,
     }

@@ -156,6 +156,19 @@ NPU_B200_API size_t npu_b200_packed_weight_bytes(int n_rows, int k);
 NPU_B200_API int npu_b200_pack_weight(const void* d_w, int n_rows, int k, void* d_packed,
                                       void* stream);
 
+/* Pack n_src_rows rows of d_w into rows of an existing panel buffer of dst_rows
+ * rows (zero-filled by the caller), so several tensors can share one buffer in
+ * the row orders the fused epilogues read:
+ *   IDENTITY    source row i -> row row_offset + i
+ *   INTERLEAVE  source row i -> row 2i + row_offset (gate with offset 0, up with 1)
+ *   HEAD_PAIRS  whole 128-row heads; head dim d -> row 2d (d < 64) or 2(d - 64) + 1,
+ *               after row_offset (a multiple of 128). */
+#define NPU_B200_PACK_IDENTITY 0
+#define NPU_B200_PACK_INTERLEAVE 1
+#define NPU_B200_PACK_HEAD_PAIRS 2
+NPU_B200_API int npu_b200_pack_weight_rows(const void* d_w, int n_src_rows, int k, void* d_packed,
+                                           int dst_rows, int order, int row_offset, void* stream);
+
 /* Projection with a fused epilogue (the decode runtime's building block,
  * exposed for kernel-level use and tests).  acc[b, n] = sum_k x[b, k] w[n, k]
  * in FP32, times rn[b] = rsqrt(sum_p ssq_in[p * ssq_ld + b] / hidden + ssq_eps) when
@@ -163,14 +176,22 @@ NPU_B200_API int npu_b200_pack_weight(const void* d_w, int n_rows, int k, void* 
  *   STORE   out[b * ld_out + n] = act(acc + bias[n])                (FP16 or FP32)
  *   RESID   h = resid[b * ld_resid + n] + acc; resid = h;
  *           xw[b * ld_xw + n] = fp16(h * norm_w[n]);
- *           ssq_out[(n / 128) * ssq_out_ld + b] = sum over the tile's rows of h^2
- *   SWIGLU  rows in [gate 64 | up 64] blocks: out[b * ld_out + j] = silu(gate_j) * up_j
- *   QKV     rows = [q_heads | kv_heads | kv_heads] x 128: optional per-head RMSNorm
- *           (q_norm_w / k_norm_w, qk_eps), RoPE at positions[b] (inv_freq[64]),
+ *           ssq_out[(n / R) * ssq_out_ld + b] = sum of h^2 over R rows,
+ *           R = ssq_out_rows (128 or 16; 0 means 128)
+ *   SWIGLU  gate and up rows interleaved: row 2j holds gate_j, row 2j + 1 up_j
+ *           (pack_weight of [gate; up] with NPU_B200_PACK_INTERLEAVE);
+ *           out[b * ld_out + j] = silu(gate_j) * up_j
+ *   QKV     rows = [q_heads | kv_heads | kv_heads] x 128, each head's rows in
+ *           rotary pair order: dims d and d + 64 are rows 2d and 2d + 1
+ *           (NPU_B200_PACK_HEAD_PAIRS); optional per-head RMSNorm (q_norm_w /
+ *           k_norm_w, qk_eps), RoPE (rotate-half) at positions[b] (inv_freq[64]),
  *           q -> out[b * ld_out + head * 128 + d], k / v -> cache
  *           [b][head][positions[b]][d] of [batch][kv_heads][max_seq][128]
- *   ARGMAX  per 128-row tile: am_val / am_idx[tile * am_ld + b] = max / argmax of acc
- *           over the tile's valid rows (lowest row on ties). */
+ *   ARGMAX  per R = am_rows rows (128 or 16; 0 means 128):
+ *           am_val / am_idx[(n / R) * am_ld + b] = max / argmax of acc over those
+ *           rows (lowest row on ties).
+ * Batches of 1-2 with packed weights, 16-row partials and no QK-norm run a
+ * CUDA-core GEMV (no workspace used); the rest run on the tensor cores. */
 enum {
   NPU_B200_EPI_STORE = 0,
   NPU_B200_EPI_RESID = 1,
@@ -205,6 +226,8 @@ typedef struct npu_b200_epilogue {
   float* am_val;
   int32_t* am_idx;
   int am_ld;
+  int ssq_out_rows;
+  int am_rows;
 } npu_b200_epilogue;
 NPU_B200_API int npu_b200_projection(const void* d_x, const void* d_w, int w_packed, int batch,
                                      int n_rows, int k, const npu_b200_epilogue* epilogue,

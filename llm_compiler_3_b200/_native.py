@@ -58,6 +58,8 @@ _SIGNATURES = [
       c_void_p]),
     ("npu_b200_packed_weight_bytes", c_size_t, [c_int, c_int]),
     ("npu_b200_pack_weight", c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    ("npu_b200_pack_weight_rows", c_int,
+     [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p]),
     ("npu_b200_projection", c_int,
      [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("npu_b200_nccl_unique_id", c_int, [c_void_p]),
@@ -82,6 +84,7 @@ LINEAR_OUT_F32 = 2
 LINEAR_PACKED_W = 4
 
 EPI_STORE, EPI_RESID, EPI_SWIGLU, EPI_QKV, EPI_ARGMAX = range(5)
+PACK_IDENTITY, PACK_INTERLEAVE, PACK_HEAD_PAIRS = range(3)
 
 
 class Epilogue(ctypes.Structure):
@@ -96,6 +99,7 @@ class Epilogue(ctypes.Structure):
         ("positions", c_void_p), ("inv_freq", c_void_p), ("k_cache", c_void_p),
         ("v_cache", c_void_p), ("max_seq", c_int), ("q_norm_w", c_void_p), ("k_norm_w", c_void_p),
         ("qk_eps", c_float), ("am_val", c_void_p), ("am_idx", c_void_p), ("am_ld", c_int),
+        ("ssq_out_rows", c_int), ("am_rows", c_int),
     ]
 
 _lib = None

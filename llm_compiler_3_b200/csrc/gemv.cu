@@ -1,0 +1,394 @@
+// Decode GEMV for one or two tokens, sm_100a: y[b, n] = sum_k W[n, k] x[b, k]
+// on CUDA cores with FP32 accumulation, plus the same fused epilogues as the
+// tensor-core projection (proj.cu).
+//
+// At batch 1-2 a projection is a pure weight stream (2 bytes per FMA), so the
+// tensor-core path's machinery -- TMEM accumulators, split-K partials, cluster
+// reductions -- is overhead.  Here the weight rows are cut into 16-row groups:
+// in every 16 KB panel (128 rows x 64 columns, the layout pack_weight writes) a
+// group's rows are one contiguous 2 KB slice, so a group never shares a row
+// with another CTA: no split-K, no fix-up.  The grid is one wave of persistent
+// CTAs, each walking a balanced share of the groups.  In every CTA one
+// producer warp streams the slices with bulk copies, four panels (8 KB) per
+// ring stage, a ring deep enough to keep ~64 KB in flight per CTA.  Each of
+// four consumer warps takes one panel of a stage: the group's 16 rows are
+// exactly the M of mma.sync m16n8k16 (A fetched with ldmatrix from the
+// swizzled slice, the one or two tokens in N = 8, FP32 accumulators), which
+// costs ~10x fewer instructions per byte than FMA-ing converted halves.  At
+// the end of a group the four warps' partial sums are added in a fixed order
+// and eight threads per row run the epilogue; a row's RoPE / SwiGLU partner
+// (the adjacent row in the packed order) is eight lanes away.
+//
+// Replaces, like proj.cu, the NPU matmul lowering
+// (lib/Transforms/HardwareOps.cpp:105-155, lib/Transforms/Emit.cpp:348-378)
+// with FP16 operands and FP32 accumulation (lib/Transforms/Normalize.cpp:123-192).
+#include <math.h>
+
+#include "common.cuh"
+#include "host.hpp"
+#include "proj.cuh"
+
+namespace npu_b200 {
+namespace {
+
+constexpr int kRows = 16;                  // rows per group
+constexpr int kParts = 8;                  // consumer threads per row
+constexpr int kConsumers = kRows * kParts; // 128: warps 0-3
+constexpr int kGemvThreads = kConsumers + 32;  // + producer warp 4
+constexpr int kPanelsPerStage = 4;
+constexpr int kSlice = kRows * 128;        // bytes of one group's slice of a panel
+constexpr int kStageBytes = kPanelsPerStage * kSlice;
+constexpr int kGemvStages = 8;
+constexpr int kGemvSmemPerSm = 233472;     // usable shared memory per SM
+constexpr int kGemvSmemReserved = 1024;    // per CTA, taken by the runtime
+
+// Barrier of the four consumer warps (named barrier 1; the producer warp never
+// takes part).
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumers) : "memory");
+}
+__device__ __forceinline__ bool consumer_sync_or(bool pred) {
+  uint32_t any;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(any)
+      : "r"(static_cast<uint32_t>(pred)), "r"(kConsumers)
+      : "memory");
+  return any != 0;
+}
+
+// Bounded wait that also gives up as soon as another warp raised the abort
+// flag; only running out of polls is reported as a device error.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase,
+                                              const volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (*abort_flag) return false;
+  }
+  report_error(kDevErrTmaTimeout);
+  return false;
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+template <int BT>
+__global__ void __launch_bounds__(kGemvThreads)
+    gemv_kernel(const uint8_t* __restrict__ w_packed, const __half* __restrict__ x,
+                const __grid_constant__ EpiParams ep, int k, int kblocks, int n_groups) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;
+  __half* xs = reinterpret_cast<__half*>(ring + kGemvStages * kStageBytes);  // [BT][k]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs + BT * k);
+  uint64_t* empty = full + kGemvStages;
+  float* part_sum = reinterpret_cast<float*>(empty + kGemvStages);  // [4 warps][16 rows][2]
+  float* red = part_sum + 4 * kRows * 2;                        // [4 warps][BT]
+  int* red_id = reinterpret_cast<int*>(red + 4 * BT);          // [4 warps][BT]
+  float* rn = reinterpret_cast<float*>(red_id + 4 * BT);       // [BT] RMSNorm scale
+  int* pos_s = reinterpret_cast<int*>(rn + BT);                // [BT] positions
+  volatile int* abort_flag = pos_s + BT;
+
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int kstages = (kblocks + kPanelsPerStage - 1) / kPanelsPerStage;
+
+  pdl_launch_dependents();
+  if (t == 0) {
+    for (int s = 0; s < kGemvStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumers / 32) {
+    // Producer: the weights never depend on the previous kernel, so it streams
+    // without waiting for it.
+    if (lane != 0) return;
+    const uint64_t pol = policy_evict_first();
+    int it = 0;
+    bool ok = true;
+    for (int g = blockIdx.x; g < n_groups && ok; g += gridDim.x) {
+      const int row0 = g * kRows;
+      const uint8_t* base =
+          w_packed + static_cast<size_t>(row0 >> 7) * kblocks * 16384 + (row0 & 127) * 128;
+      for (int ks = 0; ks < kstages; ++ks, ++it) {
+        const int s = it % kGemvStages;
+        if (!wait_or_abort(&empty[s], ((it / kGemvStages) & 1) ^ 1, abort_flag) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        const int kb0 = ks * kPanelsPerStage;
+        const int nk = min(kPanelsPerStage, kblocks - kb0);
+        mbar_arrive_expect_tx(&full[s], nk * kSlice);
+        for (int j = 0; j < nk; ++j)
+          bulk_load_hint(ring + s * kStageBytes + j * kSlice,
+                         base + static_cast<size_t>(kb0 + j) * 16384, kSlice, &full[s], pol);
+      }
+    }
+    if (!ok)  // the CTA may not exit with copies still landing in its ring
+      for (int i = max(0, it - kGemvStages); i < it; ++i)
+        mbar_wait(&full[i % kGemvStages], (i / kGemvStages) & 1, kDevErrTmaTimeout);
+    return;
+  }
+
+  // Consumers: activations, RMSNorm scale and positions of this step.
+  pdl_wait();
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(x);
+    uint4* dst = reinterpret_cast<uint4*>(xs);
+    for (int i = t; i < BT * k / 8; i += kConsumers) dst[i] = src[i];
+  }
+#pragma unroll
+  for (int b = 0; b < BT; ++b) {
+    float s = 0.f;
+    if (ep.ssq_in != nullptr && b < ep.batch)
+      for (int p = t; p < ep.ssq_parts; p += kConsumers)
+        s += ep.ssq_in[static_cast<size_t>(p) * ep.ssq_ld + b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp * BT + b] = s;
+  }
+  consumer_sync();
+  if (t < BT) {
+    const float s = red[t] + red[BT + t] + red[2 * BT + t] + red[3 * BT + t];
+    rn[t] = (ep.ssq_in != nullptr && t < ep.batch) ? rsqrtf(s * ep.ssq_inv_hidden + ep.ssq_eps) : 1.f;
+    pos_s[t] = (ep.positions != nullptr && t < ep.batch) ? ep.positions[t] : 0;
+  }
+  consumer_sync();
+
+  const int row = t / kParts, part = t % kParts;
+  const bool lead = part == 0;  // one thread per row writes
+  // ldmatrix source row / 16-byte chunk of this lane: matrix lane / 8 of the
+  // A fragment is (rows 0-7 | 8-15) x (k 0-7 | 8-15).
+  const int a_row = ((lane >> 3) & 1) * 8 + (lane & 7), a_chunk = lane >> 4;
+  const int b_tok = lane >> 2, b_k = 2 * (lane & 3);  // B fragment: token, k pair
+  int it = 0;
+  for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    bool bad = false;
+    for (int ks = 0; ks < kstages; ++ks, ++it) {
+      const int s = it % kGemvStages;
+      if (!bad && !wait_or_abort(&full[s], (it / kGemvStages) & 1, abort_flag)) {
+        bad = true;
+        *abort_flag = 1;
+      }
+      const int kb = ks * kPanelsPerStage + warp;  // this warp's panel
+      if (!bad && kb < kblocks) {
+        const uint32_t slice = smem_u32(ring + s * kStageBytes + warp * kSlice) + a_row * 128;
+        const __half* xk = xs + kb * 64 + b_k;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t a0, a1, a2, a3, b0 = 0, b1 = 0;
+          ldmatrix_x4(a0, a1, a2, a3, slice + (((2 * kk + a_chunk) ^ (a_row & 7)) << 4));
+          if (b_tok < BT) {
+            b0 = *reinterpret_cast<const uint32_t*>(xk + b_tok * k + kk * 16);
+            b1 = *reinterpret_cast<const uint32_t*>(xk + b_tok * k + kk * 16 + 8);
+          }
+          mma_16816(c, a0, a1, a2, a3, b0, b1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (consumer_sync_or(bad)) return;
+
+    // Add the four warps' sums (lanes 4i hold rows i and i + 8, tokens 0-1).
+    if ((lane & 3) == 0) {
+      float* ps = part_sum + warp * kRows * 2;
+      ps[(lane >> 2) * 2] = c[0];
+      ps[(lane >> 2) * 2 + 1] = c[1];
+      ps[((lane >> 2) + 8) * 2] = c[2];
+      ps[((lane >> 2) + 8) * 2 + 1] = c[3];
+    }
+    consumer_sync();
+    float acc[BT];
+#pragma unroll
+    for (int b = 0; b < BT; ++b)
+      acc[b] = (((part_sum[row * 2 + b] + part_sum[(kRows + row) * 2 + b]) +
+                 part_sum[(2 * kRows + row) * 2 + b]) +
+                part_sum[(3 * kRows + row) * 2 + b]) *
+               rn[b];
+    const int n = g * kRows + row;         // row of W
+    const int tile = n >> 7, p = n & 127;  // 128-row tile and row within it
+
+    if (ep.kind == kEpiStore) {
+      if (lead) {
+        const float bias = ep.bias ? __half2float(ep.bias[n]) : 0.f;
+#pragma unroll
+        for (int b = 0; b < BT; ++b) {
+          if (b < ep.batch) {
+            float v = acc[b] + bias;
+            if (ep.relu) v = fmaxf(v, 0.f);
+            const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
+            if (ep.out_f32)
+              static_cast<float*>(ep.out)[off] = v;
+            else
+              static_cast<__half*>(ep.out)[off] = __float2half_rn(v);
+          }
+        }
+      }
+    } else if (ep.kind == kEpiResid) {
+      // Residual add, next norm's input, and the group's sum of squares.
+      const float w = __half2float(ep.norm_w[n]);
+#pragma unroll
+      for (int b = 0; b < BT; ++b) {
+        float h2 = 0.f;
+        if (lead && b < ep.batch) {
+          const size_t off = static_cast<size_t>(b) * ep.ld_resid + n;
+          const float h = ep.resid[off] + acc[b];
+          ep.resid[off] = h;
+          ep.xw[static_cast<size_t>(b) * ep.ld_xw + n] = __float2half_rn(h * w);
+          h2 = h * h;
+        }
+#pragma unroll
+        for (int o = kParts; o < 32; o <<= 1) h2 += __shfl_xor_sync(0xffffffffu, h2, o);
+        if (lane == 0) red[warp * BT + b] = h2;
+      }
+      consumer_sync();
+      if (t < BT && t < ep.batch)
+        ep.ssq_out[static_cast<size_t>(g) * ep.ssq_out_ld + t] =
+            red[t] + red[BT + t] + red[2 * BT + t] + red[3 * BT + t];
+    } else if (ep.kind == kEpiSwiGLU) {
+      // (gate_j, up_j) are rows (2j, 2j + 1).
+#pragma unroll
+      for (int b = 0; b < BT; ++b) {
+        const float up = __shfl_xor_sync(0xffffffffu, acc[b], kParts);
+        if (lead && (n & 1) == 0 && b < ep.batch) {
+          const float gt = acc[b];
+          static_cast<__half*>(ep.out)[static_cast<size_t>(b) * ep.ld_out + (n >> 1)] =
+              __float2half_rn(gt / (1.f + expf(-gt)) * up);
+        }
+      }
+    } else if (ep.kind == kEpiQKV) {
+      // Head rows in pair order: row p holds dim (p >> 1) + 64 * (p & 1).
+      const bool is_q = tile < ep.q_heads;
+      const bool is_k = !is_q && tile < ep.q_heads + ep.kv_heads;
+      const int i = p >> 1, d = i + ((p & 1) << 6);
+#pragma unroll
+      for (int b = 0; b < BT; ++b) {
+        const float partner = __shfl_xor_sync(0xffffffffu, acc[b], kParts);
+        if ((is_q || is_k) && b < ep.batch) {
+          float sn, cs;
+          if (ep.rope_tab != nullptr) {
+            const float2 cssn = reinterpret_cast<const float2*>(ep.rope_tab)[b * 64 + i];
+            cs = cssn.x;
+            sn = cssn.y;
+          } else {
+            sincosf(static_cast<float>(pos_s[b]) * ep.inv_freq[i], &sn, &cs);
+          }
+          acc[b] = (p & 1) == 0 ? acc[b] * cs - partner * sn : acc[b] * cs + partner * sn;
+        }
+      }
+      if (lead) {
+#pragma unroll
+        for (int b = 0; b < BT; ++b) {
+          if (b >= ep.batch) continue;
+          if (is_q) {
+            static_cast<__half*>(ep.out)[static_cast<size_t>(b) * ep.ld_out + tile * 128 + d] =
+                __float2half_rn(acc[b]);
+          } else {
+            const int kh = is_k ? tile - ep.q_heads : tile - ep.q_heads - ep.kv_heads;
+            const int pos = pos_s[b];
+            if (pos < 0 || pos >= ep.max_seq) {
+              report_error(kDevErrBounds);
+            } else {
+              __half* cache = is_k ? ep.k_cache : ep.v_cache;
+              cache[static_cast<size_t>(b) * ep.cache_batch_stride +
+                    (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + d] = __float2half_rn(acc[b]);
+            }
+          }
+        }
+      }
+    } else if (ep.kind == kEpiArgmax) {
+      // The group's (max, argmax) per token, lowest row on ties.
+#pragma unroll
+      for (int b = 0; b < BT; ++b) {
+        float bv = lead ? acc[b] : -INFINITY;
+        int bi = n;
+#pragma unroll
+        for (int o = kParts; o < 32; o <<= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) {
+          red[warp * BT + b] = bv;
+          red_id[warp * BT + b] = bi;
+        }
+      }
+      consumer_sync();
+      if (t < BT && t < ep.batch) {
+        float bv = red[t];
+        int bi = red_id[t];
+        for (int w = 1; w < 4; ++w)
+          if (better(red[w * BT + t], red_id[w * BT + t], bv, bi)) {
+            bv = red[w * BT + t];
+            bi = red_id[w * BT + t];
+          }
+        ep.am_val[static_cast<size_t>(g) * ep.am_ld + t] = bv;
+        ep.am_idx[static_cast<size_t>(g) * ep.am_ld + t] = bi;
+      }
+    }
+  }
+}
+
+template <int BT>
+size_t gemv_smem(int k) {
+  // ring + staged activations + full/empty barriers + reduction scratch
+  return static_cast<size_t>(kGemvStages) * kStageBytes + static_cast<size_t>(BT) * k * 2 +
+         2 * kGemvStages * 8 + (4 * kRows * 2 + 4 * BT + 4 * BT + BT + BT + 1) * 4 + 64;
+}
+
+template <int BT>
+int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams& ep,
+                cudaStream_t stream, bool pdl) {
+  const size_t smem = gemv_smem<BT>(k);
+  auto kern = gemv_kernel<BT>;
+  NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  // One wave of persistent CTAs, as many per SM as shared memory allows, and
+  // the groups spread so that every CTA walks the same number (+-1).
+  const int per_sm = max(1, min(8, kGemvSmemPerSm / static_cast<int>(smem + kGemvSmemReserved)));
+  const int n_groups = n_rows / kRows;
+  const int slots = per_sm * sm_count();
+  const int rounds = (n_groups + slots - 1) / slots;
+  LaunchCfg cfg;
+  cfg.grid = dim3((n_groups + rounds - 1) / rounds);
+  cfg.block = dim3(kGemvThreads);
+  cfg.smem = smem;
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, kern, static_cast<const uint8_t*>(w), static_cast<const __half*>(x), ep, k,
+                k / 64, n_groups);
+}
+
+}  // namespace
+
+bool gemv_supported(int n_rows, int k, int batch, const EpiParams& ep) {
+  if (batch < 1 || batch > 2 || n_rows < kRows || n_rows % kRows != 0 || k < 64 || k % 64 != 0)
+    return false;
+  if (static_cast<size_t>(batch) * k * 2 > 64 * 1024) return false;  // staged activations
+  if (ep.kind == kEpiQKV && (ep.q_norm_w != nullptr || ep.k_norm_w != nullptr)) return false;
+  if (ep.kind == kEpiResid && ep.ssq_out_rows != kRows) return false;
+  if (ep.kind == kEpiArgmax && ep.am_rows != kRows) return false;
+  return true;
+}
+
+int gemv_run(const void* w_packed, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
+             cudaStream_t stream, bool pdl) {
+  NPU_REQUIRE(gemv_supported(n_rows, k, batch, ep), "gemv: unsupported shape or epilogue");
+  NPU_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0, "gemv: x must be 16-byte aligned");
+  return batch == 1 ? launch_gemv<1>(w_packed, x, n_rows, k, ep, stream, pdl)
+                    : launch_gemv<2>(w_packed, x, n_rows, k, ep, stream, pdl);
+}
+
+}  // namespace npu_b200

@@ -191,33 +191,45 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
       tile_s[q * P + r] = h2;
     }
     epi_sync();
-    column_sums(tile_s, aux);
-    epi_sync();
-    if (r < kChunkCols && b0 + r < batch)
-      ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + b0 + r] = aux[r];
-    epi_sync();
-  } else if (ep.kind == kEpiSwiGLU) {
-#pragma unroll
-    for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = v[q];
-    epi_sync();
-    const int j = tile * 64 + r;
-    if (r < 64 && j < ep.n_rows / 2) {
+    if (ep.ssq_out_rows == 16) {
+      // One partial per 16 rows: warp w sums rows 16g..16g+15 (g = 2w, 2w+1)
+      // for every token of the chunk, half a warp per group.
+      const int warp = r >> 5, lane = r & 31;
+      const int g = 2 * warp + (lane >> 4), row = lane & 15;
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q) {
-        const int b = b0 + q;
-        if (b < batch) {
-          const float g = tile_s[q * P + r];
-          const float u = tile_s[q * P + r + 64];
-          const float act = g / (1.f + expf(-g)) * u;
-          static_cast<__half*>(ep.out)[static_cast<size_t>(b) * ep.ld_out + j] =
-              __float2half_rn(act);
-        }
+        float t = tile_s[q * P + 16 * g + row];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (row == 0 && b0 + q < batch && tile * 128 + 16 * g < ep.n_rows)
+          ep.ssq_out[static_cast<size_t>(tile * 8 + g) * ep.ssq_out_ld + b0 + q] = t;
       }
+    } else {
+      column_sums(tile_s, aux);
+      epi_sync();
+      if (r < kChunkCols && b0 + r < batch)
+        ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + b0 + r] = aux[r];
     }
     epi_sync();
+  } else if (ep.kind == kEpiSwiGLU) {
+    // Rows come in (gate_j, up_j) pairs: even row r holds gate, r + 1 holds up,
+    // j = tile * 64 + r / 2.  The partner is the neighbouring lane.
+    const int j = tile * 64 + (r >> 1);
+#pragma unroll
+    for (int q = 0; q < kChunkCols; ++q) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[q], 1);
+      if ((r & 1) == 0 && b0 + q < batch && j < ep.n_rows / 2) {
+        const float g = v[q], u = other;
+        static_cast<__half*>(ep.out)[static_cast<size_t>(b0 + q) * ep.ld_out + j] =
+            __float2half_rn(g / (1.f + expf(-g)) * u);
+      }
+    }
   } else if (ep.kind == kEpiQKV) {
+    // Head tiles store head dims in rotate_half pair order: row r holds dim
+    // d = r / 2 + 64 * (r % 2), so RoPE partners (d, d + 64) are adjacent lanes.
     const bool is_q = tile < ep.q_heads;
     const bool is_k = !is_q && tile < ep.q_heads + ep.kv_heads;
+    const int d = (r >> 1) + ((r & 1) << 6);
     const __half* nw = is_q ? ep.q_norm_w : (is_k ? ep.k_norm_w : nullptr);
     if (nw) {  // per-head RMSNorm over the 128 dims (Qwen3 q_norm / k_norm)
 #pragma unroll
@@ -227,39 +239,36 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
       epi_sync();
       if (r < kChunkCols) aux[r] = rsqrtf(aux[r] * (1.f / 128.f) + ep.qk_eps);
       epi_sync();
-      const float wr = __half2float(nw[r]);
+      const float wr = __half2float(nw[d]);
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q) v[q] = v[q] * aux[q] * wr;
-    }
-    if (is_q || is_k) {  // RoPE: rotate_half pairs (i, i + 64)
-#pragma unroll
-      for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = v[q];
       epi_sync();
-      const float f = ep.inv_freq[r & 63];
+    }
+    if (is_q || is_k) {  // RoPE: out_d = x_d cos - x_{d+64} sin, out_{d+64} = x_{d+64} cos + x_d sin
+      const int i = r >> 1;
+      const float f = ep.inv_freq[i];
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[q], 1);
         if (b0 + q < batch) {
-          const float partner = tile_s[q * P + (r ^ 64)];
           float sn, cs;
           if (ep.rope_tab != nullptr) {  // cos / sin of this step's positions, precomputed
-            const float2 cssn =
-                reinterpret_cast<const float2*>(ep.rope_tab)[(b0 + q) * 64 + (r & 63)];
+            const float2 cssn = reinterpret_cast<const float2*>(ep.rope_tab)[(b0 + q) * 64 + i];
             cs = cssn.x;
             sn = cssn.y;
           } else {
             sincosf(static_cast<float>(pos_s[b0 + q]) * f, &sn, &cs);
           }
-          v[q] = r < 64 ? v[q] * cs - partner * sn : v[q] * cs + partner * sn;
+          v[q] = (r & 1) == 0 ? v[q] * cs - partner * sn : v[q] * cs + partner * sn;
         }
       }
-      epi_sync();
     }
     if (is_q) {
       __half* qo = static_cast<__half*>(ep.out);
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q)
         if (b0 + q < batch)
-          qo[static_cast<size_t>(b0 + q) * ep.ld_out + tile * 128 + r] = __float2half_rn(v[q]);
+          qo[static_cast<size_t>(b0 + q) * ep.ld_out + tile * 128 + d] = __float2half_rn(v[q]);
     } else {
       const int kh = is_k ? tile - ep.q_heads : tile - ep.q_heads - ep.kv_heads;
       __half* cache = is_k ? ep.k_cache : ep.v_cache;
@@ -272,7 +281,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
             if (r == 0) report_error(kDevErrBounds);
           } else {
             cache[static_cast<size_t>(b) * ep.cache_batch_stride +
-                  (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + r] = __float2half_rn(v[q]);
+                  (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + d] = __float2half_rn(v[q]);
           }
         }
       }
@@ -283,12 +292,37 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
 #pragma unroll
     for (int q = 0; q < kChunkCols; ++q) tile_s[q * P + r] = valid ? v[q] : -INFINITY;
     epi_sync();
-    int* aux_i = reinterpret_cast<int*>(aux) + kChunkCols;
-    column_argmax(tile_s, tile * 128, aux, aux_i);
-    epi_sync();
-    if (r < kChunkCols && b0 + r < batch) {
-      ep.am_val[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = aux[r];
-      ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = aux_i[r];
+    if (ep.am_rows == 16) {
+      // One (max, argmax) per 16 rows, half a warp per group as for the sums.
+      const int warp = r >> 5, lane = r & 31;
+      const int g = 2 * warp + (lane >> 4), row = lane & 15;
+#pragma unroll
+      for (int q = 0; q < kChunkCols; ++q) {
+        float bv = tile_s[q * P + 16 * g + row];
+        int bi = row;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (row == 0 && b0 + q < batch && tile * 128 + 16 * g < ep.n_rows) {
+          const size_t at = static_cast<size_t>(tile * 8 + g) * ep.am_ld + b0 + q;
+          ep.am_val[at] = bv;
+          ep.am_idx[at] = tile * 128 + 16 * g + bi;
+        }
+      }
+    } else {
+      int* aux_i = reinterpret_cast<int*>(aux) + kChunkCols;
+      column_argmax(tile_s, tile * 128, aux, aux_i);
+      epi_sync();
+      if (r < kChunkCols && b0 + r < batch) {
+        ep.am_val[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = aux[r];
+        ep.am_idx[static_cast<size_t>(tile) * ep.am_ld + b0 + r] = aux_i[r];
+      }
     }
     epi_sync();
   }
@@ -775,7 +809,12 @@ __global__ void pack_panels_kernel(const __half* __restrict__ src, size_t src_pi
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const int i = static_cast<int>(idx / chunks), c = static_cast<int>(idx % chunks);
-    const int row = row_mode == 0 ? row_offset + i : (i / 64) * 128 + (i % 64) + row_offset;
+    // 0: identity; 1: gate/up interleave (row 2i + offset); 2: head dims in
+    // rotate_half pair order (dim d of a 128-row head -> row 2d or 2(d-64)+1).
+    const int hd = i & 127;
+    const int row = row_mode == 0   ? row_offset + i
+                    : row_mode == 1 ? 2 * i + row_offset
+                                    : row_offset + (i & ~127) + (hd < 64 ? 2 * hd : 2 * (hd - 64) + 1);
     const int t = row >> 7, r = row & 127, kb = c >> 3, j = c & 7;
     const size_t off = (static_cast<size_t>(t) * kblocks + kb) * 16384 + r * 128 + ((j ^ (r & 7)) << 4);
     *reinterpret_cast<uint4*>(dst + off) =
@@ -804,8 +843,10 @@ int pack_weight(const void* src, size_t src_pitch, int n_src_rows, int k, void* 
   NPU_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (src_pitch * 2) % 16 == 0 &&
                   (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
               "pack: source rows and destination must be 16-byte aligned");
-  const int last = row_mode == 0 ? row_offset + n_src_rows - 1
-                                 : ((n_src_rows - 1) / 64) * 128 + ((n_src_rows - 1) % 64) + row_offset;
+  NPU_REQUIRE(row_mode >= 0 && row_mode <= 2, "pack: unknown row mode %d", row_mode);
+  NPU_REQUIRE(row_mode != 2 || (n_src_rows % 128 == 0 && row_offset % 128 == 0),
+              "pack: head-pair order needs whole 128-row heads");
+  const int last = row_mode == 1 ? 2 * (n_src_rows - 1) + row_offset : row_offset + n_src_rows - 1;
   NPU_REQUIRE(row_offset >= 0 && last < ((dst_rows + 127) / 128) * 128,
               "pack: rows land outside the destination");
   LaunchCfg cfg;
@@ -839,12 +880,23 @@ int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int
   if (ep.kind == kEpiResid)
     NPU_REQUIRE(ep.resid && ep.norm_w && ep.xw && ep.ssq_out,
                 "projection: residual epilogue needs resid, norm weight, xw and ssq outputs");
-  if (ep.kind == kEpiArgmax) NPU_REQUIRE(ep.am_val && ep.am_idx, "projection: argmax outputs");
+  if (ep.kind == kEpiArgmax)
+    NPU_REQUIRE(ep.am_val && ep.am_idx && ep.am_ld >= batch && (ep.am_rows == 16 || ep.am_rows == 128),
+                "projection: argmax outputs need am_ld >= batch and 16 or 128 rows per partial");
+  if (ep.kind == kEpiResid)
+    NPU_REQUIRE(ep.ssq_out_ld >= batch && (ep.ssq_out_rows == 16 || ep.ssq_out_rows == 128),
+                "projection: sums of squares need ssq_out_ld >= batch and 16 or 128 rows per partial");
   if (ep.kind == kEpiStore) NPU_REQUIRE(ep.out != nullptr, "projection: null output");
   NPU_REQUIRE(ep.kind >= kEpiStore && ep.kind <= kEpiArgmax, "projection: unknown epilogue %d",
               ep.kind);
   NPU_REQUIRE(ep.ssq_in == nullptr || (ep.ssq_parts >= 1 && ep.ssq_ld >= batch),
               "projection: RMSNorm input needs ssq_parts >= 1 and ssq_ld >= batch");
+
+  if (w_packed && gemv_supported(n_rows, k, batch, ep))
+    return gemv_run(w, x, n_rows, k, batch, ep, stream, pdl);
+
+  if (w_packed && gemv_supported(n_rows, k, batch, ep))
+    return gemv_run(w, x, n_rows, k, batch, ep, stream, pdl);
 
   const Geometry g = geometry(n_rows, k, batch);
   const size_t need = g.counter_bytes + g.slot_bytes;
@@ -890,6 +942,16 @@ extern "C" int npu_b200_pack_weight(const void* d_w, int n_rows, int k, void* d_
   NPU_REQUIRE(d_packed, "pack: null destination");
   NPU_TRY_CUDA(cudaMemsetAsync(d_packed, 0, packed_weight_bytes(n_rows, k), s));
   return pack_weight(d_w, static_cast<size_t>(k), n_rows, k, d_packed, n_rows, 0, 0, s);
+}
+
+extern "C" int npu_b200_pack_weight_rows(const void* d_w, int n_src_rows, int k, void* d_packed,
+                                         int dst_rows, int order, int row_offset, void* stream) {
+  clear_error();
+  NPU_REQUIRE(order == NPU_B200_PACK_IDENTITY || order == NPU_B200_PACK_INTERLEAVE ||
+                  order == NPU_B200_PACK_HEAD_PAIRS,
+              "pack: unknown row order %d", order);
+  return pack_weight(d_w, static_cast<size_t>(k), n_src_rows, k, d_packed, dst_rows, order,
+                     row_offset, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int npu_b200_linear(const void* d_x, const void* d_w, const void* d_bias, void* d_out,
@@ -952,6 +1014,8 @@ extern "C" int npu_b200_projection(const void* d_x, const void* d_w, int w_packe
   ep.am_val = e->am_val;
   ep.am_idx = e->am_idx;
   ep.am_ld = e->am_ld;
+  ep.ssq_out_rows = e->ssq_out_rows == 0 ? 128 : e->ssq_out_rows;
+  ep.am_rows = e->am_rows == 0 ? 128 : e->am_rows;
   NPU_REQUIRE(ep.ssq_in == nullptr || e->hidden > 0, "projection: RMSNorm input needs hidden");
   return proj_run(d_w, w_packed != 0, d_x, n_rows, k, batch, ep, d_workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), false);

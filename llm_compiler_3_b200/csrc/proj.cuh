@@ -12,8 +12,9 @@ namespace npu_b200 {
 enum EpiKind : int {
   kEpiStore = 0,   // out[b, n] = acc (+ bias[n]) (ReLU), FP16 or FP32
   kEpiResid = 1,   // h = resid + acc; resid = h; xw = fp16(h * norm_w); ssq partial of h
-  kEpiSwiGLU = 2,  // rows [gate 64 | up 64] per tile: act[b, j] = silu(gate) * up
-  kEpiQKV = 3,     // per-head tiles: [QK-norm], RoPE, write q / append k,v to the cache
+  kEpiSwiGLU = 2,  // rows (gate_j, up_j) interleaved: act[b, j] = silu(gate_j) * up_j
+  kEpiQKV = 3,     // per-head tiles (dims in rotate_half pair order): [QK-norm], RoPE,
+                   // write q / append k,v to the cache
   kEpiArgmax = 4,  // per-tile (max, argmax) over rows for every token
 };
 
@@ -43,8 +44,9 @@ struct EpiParams {
   const __half* norm_w = nullptr;
   __half* xw = nullptr;
   int ld_xw = 0;
-  float* ssq_out = nullptr;  // [tile][ssq_out_ld]
+  float* ssq_out = nullptr;  // [n / ssq_out_rows][ssq_out_ld]
   int ssq_out_ld = 0;
+  int ssq_out_rows = 128;    // rows per partial sum: 128 or 16
 
   // kEpiQKV (head_dim 128: one tile is one head)
   int q_heads = 0, kv_heads = 0;
@@ -60,9 +62,10 @@ struct EpiParams {
   float qk_eps = 0.f;
 
   // kEpiArgmax: part_val/part_idx [tile][batch]
-  float* am_val = nullptr;
+  float* am_val = nullptr;    // [ceil(n / am_rows)][am_ld]
   int32_t* am_idx = nullptr;
   int am_ld = 0;
+  int am_rows = 128;          // rows per partial (max, argmax): 128 or 16
 };
 
 // Runs the projection.  w is [n_rows, k] FP16 row-major, or (w_packed) the
@@ -73,14 +76,22 @@ int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int
              bool pdl);
 size_t proj_workspace_bytes(int n_rows, int k, int batch);
 
+// Batch 1-2 GEMV over packed panels (gemv.cu): no workspace.  Supported when
+// n_rows % 16 == 0, the activations fit in shared memory, no QK-norm, and a
+// residual epilogue writes 16-row sums of squares.
+bool gemv_supported(int n_rows, int k, int batch, const EpiParams& ep);
+int gemv_run(const void* w_packed, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
+             cudaStream_t stream, bool pdl);
+
 // Weight panels: 16 KB blocks [ceil(n/128)][k/64] of 128 rows x 64 columns,
 // each already in the 128-byte-swizzled K-major layout the tensor cores read,
 // so one contiguous bulk copy moves a block from HBM to shared memory.
 size_t packed_weight_bytes(int n_rows, int k);
 // Packs n_src_rows source rows (row pitch src_pitch elements) into a panel
 // buffer of dst_rows rows.  row_mode 0: destination row = row_offset + i;
-// row_mode 1: rows interleave per 64 into 128-row tiles, [gate 64 | up 64]:
-// destination row = (i / 64) * 128 + i % 64 + row_offset (row_offset 0 or 64).
+// row_mode 1: gate/up interleave, destination row = 2 i + row_offset (0 or 1);
+// row_mode 2: whole 128-row heads with dims in rotate_half pair order,
+// dim d -> row 2d (d < 64) or 2(d - 64) + 1, after row_offset.
 int pack_weight(const void* src, size_t src_pitch, int n_src_rows, int k, void* dst, int dst_rows,
                 int row_mode, int row_offset, cudaStream_t stream);
 

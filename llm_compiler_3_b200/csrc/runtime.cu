@@ -18,6 +18,9 @@
 //               proj[down: + residual, xw = h*w_next, ssq]     (TP: -> all-reduce)
 //   proj[LM head: rms scale, per-tile argmax] -> argmax_reduce (TP: all-gather)
 //
+// At batch 1-2 every proj runs as the CUDA-core GEMV (gemv.cu) and the sums of
+// squares and partial argmaxes are kept per 16 rows; above, on the tensor
+// cores with per-128-row partials.
 // Every kernel is launched with programmatic dependent launch, so the next
 // projection starts streaming its weights while the previous kernel drains.
 #include <dlfcn.h>
@@ -371,15 +374,16 @@ int allocate(npu_b200_ctx* c) {
         (rc = dalloc(c, H, &c->final_norm, false)) ||
         (rc = dalloc(c, packed_weight_bytes(c->vocab_loc, static_cast<int>(H)) / 2, &c->lm_head)))
       return rc;
-    const int lm_tiles = (c->vocab_loc + 127) / 128;
-    if ((rc = dalloc(c, static_cast<size_t>(lm_tiles) * B, &c->am_val)) ||
-        (rc = dalloc(c, static_cast<size_t>(lm_tiles) * B, &c->am_idx)) ||
+    // Partial argmaxes: one per 16 rows at batch 1-2, per 128 rows above.
+    const int lm_parts = (c->vocab_loc + 15) / 16;
+    if ((rc = dalloc(c, static_cast<size_t>(lm_parts) * B, &c->am_val)) ||
+        (rc = dalloc(c, static_cast<size_t>(lm_parts) * B, &c->am_idx)) ||
         (rc = dalloc(c, 2 * B, &c->gather_send)) ||
         (rc = dalloc(c, 2 * B * static_cast<size_t>(T), &c->gather_recv)))
       return rc;
   }
   if ((rc = dalloc(c, B * H, &c->resid)) || (rc = dalloc(c, B * H, &c->xw)) ||
-      (rc = dalloc(c, (H / 128) * B, &c->ssq)) || (rc = dalloc(c, B * H, &c->partial)) ||
+      (rc = dalloc(c, (H / 16) * B, &c->ssq)) || (rc = dalloc(c, B * H, &c->partial)) ||
       (rc = dalloc(c, B * c->q_loc * D, &c->q_buf)) || (rc = dalloc(c, B * c->q_loc * D, &c->attn)) ||
       (rc = dalloc(c, B * c->ffn_loc, &c->act)) || (rc = dalloc(c, B * H, &c->hidden_io)) ||
       (rc = dalloc(c, B, &c->d_tokens)) || (rc = dalloc(c, B, &c->d_positions)) ||
@@ -495,7 +499,7 @@ int place_weight(npu_b200_ctx* c, int layer, int kind, const void* src, size_t b
         const int row0 = kind == kQ ? 0 : (kind == kK ? c->q_loc : c->q_loc + c->kv_loc) * Di;
         const int rows = (c->q_loc + 2 * c->kv_loc) * Di;
         if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(r) * loc * D * H,
-                              H, loc * Di, Hi, L.w_qkv, rows, 0, row0, st)))
+                              H, loc * Di, Hi, L.w_qkv, rows, 2, row0, st)))
           return rc;
         break;
       }
@@ -508,10 +512,10 @@ int place_weight(npu_b200_ctx* c, int layer, int kind, const void* src, size_t b
         break;
       }
       case kGate:
-      case kUp: {  // rows interleaved per 64 into [gate 64 | up 64] tiles
+      case kUp: {  // rows interleaved: gate_j at row 2j, up_j at row 2j + 1
         if ((rc = expect(static_cast<size_t>(P.ffn) * H)) || (rc = device_source(&d))) return rc;
         if ((rc = pack_weight(static_cast<const __half*>(d) + static_cast<size_t>(r) * c->ffn_loc * H,
-                              H, c->ffn_loc, Hi, L.w_gu, 2 * c->ffn_loc, 1, kind == kUp ? 64 : 0,
+                              H, c->ffn_loc, Hi, L.w_gu, 2 * c->ffn_loc, 1, kind == kUp ? 1 : 0,
                               st)))
           return rc;
         break;
@@ -591,9 +595,13 @@ int resolve_name(const npu_b200_ctx* c, const std::string& name, int* layer, int
 // ---------------------------------------------------------------------------
 // One decode step, enqueued on `s` (used under stream capture).
 // ---------------------------------------------------------------------------
-void norm_input(const npu_b200_ctx* c, EpiParams* e) {
+// Rows per partial sum of squares / partial argmax: 16 at batch 1-2 (the
+// shapes the GEMV runs, one partial per 16-row CTA group), 128 above.
+int part_rows(int batch) { return batch <= 2 ? 16 : 128; }
+
+void norm_input(const npu_b200_ctx* c, int batch, EpiParams* e) {
   e->ssq_in = c->ssq;
-  e->ssq_parts = c->plan.hidden / 128;
+  e->ssq_parts = c->plan.hidden / part_rows(batch);
   e->ssq_ld = c->plan.max_batch;
   e->ssq_inv_hidden = 1.f / static_cast<float>(c->plan.hidden);
   e->ssq_eps = c->plan.eps;
@@ -614,6 +622,7 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
     e.ld_xw = P.hidden;
     e.ssq_out = c->ssq;
     e.ssq_out_ld = P.max_batch;
+    e.ssq_out_rows = part_rows(batch);
     return proj_run(w, true, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
   }
   e.kind = kEpiStore;
@@ -637,6 +646,7 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
   u.xw = c->xw;
   u.ssq_out = c->ssq;
   u.ssq_ld = P.max_batch;
+  u.ssq_rows = part_rows(batch);
   return residual_update(u, s, false);
 }
 
@@ -658,6 +668,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     u.xw = c->xw;
     u.ssq_out = c->ssq;
     u.ssq_ld = P.max_batch;
+    u.ssq_rows = part_rows(batch);
     u.positions = c->d_positions;
     u.seq_lens = c->d_seq_lens;
     u.inv_freq = c->d_inv_freq;
@@ -670,7 +681,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     q.kind = kEpiQKV;
     q.n_rows = (c->q_loc + 2 * c->kv_loc) * D;
     q.batch = batch;
-    norm_input(c, &q);
+    norm_input(c, batch, &q);
     q.out = c->q_buf;
     q.ld_out = c->q_loc * D;
     q.q_heads = c->q_loc;
@@ -697,7 +708,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     g.kind = kEpiSwiGLU;
     g.n_rows = 2 * c->ffn_loc;
     g.batch = batch;
-    norm_input(c, &g);
+    norm_input(c, batch, &g);
     g.out = c->act;
     g.ld_out = c->ffn_loc;
     if ((rc = proj_run(L.w_gu, true, c->xw, g.n_rows, H, batch, g, c->proj_ws, c->proj_ws_bytes, s,
@@ -714,14 +725,15 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
   a.kind = kEpiArgmax;
   a.n_rows = c->vocab_loc;
   a.batch = batch;
-  norm_input(c, &a);
+  norm_input(c, batch, &a);
   a.am_val = c->am_val;
   a.am_idx = c->am_idx;
   a.am_ld = P.max_batch;
+  a.am_rows = part_rows(batch);
   if ((rc = proj_run(c->lm_head, true, c->xw, c->vocab_loc, H, batch, a, c->proj_ws, c->proj_ws_bytes,
                      s, true)))
     return rc;
-  const int lm_tiles = (c->vocab_loc + 127) / 128;
+  const int lm_tiles = (c->vocab_loc + a.am_rows - 1) / a.am_rows;
   if (c->tp_size == 1)
     return argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
                          c->gather_send, c->d_ids, s, true);

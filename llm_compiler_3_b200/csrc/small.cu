@@ -58,6 +58,13 @@ __global__ void __launch_bounds__(kChunk)
   p.resid[static_cast<size_t>(b) * p.hidden + n] = h;
   p.xw[static_cast<size_t>(b) * p.hidden + n] = __float2half_rn(h * w);
   float s = h * h;
+  if (p.ssq_rows == 16) {  // one sum per half warp
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((lane & 15) == 0)
+      p.ssq_out[static_cast<size_t>(blockIdx.x * 8 + warp * 2 + (lane >> 4)) * p.ssq_ld + b] = s;
+    return;
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) red[warp] = s;

@@ -25,8 +25,9 @@ struct ResidualUpdate {
   float* resid = nullptr;             // [batch, hidden]
   const __half* norm_w = nullptr;     // [hidden] weight of the RMSNorm that follows
   __half* xw = nullptr;               // [batch, hidden] fp16(h * norm_w)
-  float* ssq_out = nullptr;           // [hidden / 128][ssq_ld]
+  float* ssq_out = nullptr;           // [hidden / ssq_rows][ssq_ld]
   int ssq_ld = 0;
+  int ssq_rows = 128;                 // rows per sum of squares: 128 or 16
   const int32_t* positions = nullptr; // optional: seq_lens[b] = positions[b] + 1
   int32_t* seq_lens = nullptr;
   const float* inv_freq = nullptr;    // optional with rope_tab: [64] RoPE inverse frequencies

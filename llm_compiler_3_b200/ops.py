@@ -122,6 +122,23 @@ def pack_weight(weight: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def pack_weight_rows(parts, rows: int) -> torch.Tensor:
+    """Panels of `rows` rows assembled from (weight [n_i, K], order, row_offset)
+    parts (see npu_b200_pack_weight_rows), e.g. [(gate, PACK_INTERLEAVE, 0),
+    (up, PACK_INTERLEAVE, 1)] for the SwiGLU epilogue."""
+    k = parts[0][0].shape[1]
+    lib = _native.lib()
+    out = torch.zeros(lib.npu_b200_packed_weight_bytes(rows, k), dtype=torch.uint8,
+                      device=parts[0][0].device)
+    for weight, order, offset in parts:
+        _require(weight, "weight", ndim=2)
+        if weight.shape[1] != k:
+            raise ValueError("pack_weight_rows: parts differ in K")
+        _native.check(lib.npu_b200_pack_weight_rows(_ptr(weight), weight.shape[0], k, _ptr(out),
+                                                    rows, order, offset, _stream()))
+    return out
+
+
 def projection(x: torch.Tensor, weight: torch.Tensor, n_rows: int, epilogue,
                packed: bool = False) -> None:
     """Run npu_b200_projection with a filled _native.Epilogue (pointers set by the

@@ -33,24 +33,43 @@ def _norm_input(x32, batch, parts=4):
     return (chunks * chunks).sum(-1).t().contiguous()      # [parts, batch]
 
 
-@pytest.mark.parametrize("batch", [1, 16, 64])
+def _pair_order(w, heads):
+    """Rows of each 128-row head in rotary pair order: row 2i holds dim i,
+    row 2i + 1 dim i + 64 (NPU_B200_PACK_HEAD_PAIRS)."""
+    i = torch.arange(64)
+    perm = torch.stack([i, i + 64], 1).reshape(-1)
+    return w.view(heads, 128, -1)[:, perm].reshape(w.shape)
+
+
+def _interleave(gate, up):
+    """gate_j at row 2j, up_j at row 2j + 1 (NPU_B200_PACK_INTERLEAVE)."""
+    return torch.stack([gate, up], 1).reshape(2 * gate.shape[0], -1)
+
+
+@pytest.mark.parametrize("batch", [1, 2, 16, 64])
 @pytest.mark.parametrize("packed", [False, True])
-def test_packed_weights_bit_identical(cuda, batch, packed):
-    from llm_compiler_3_b200 import ops
-    x = seeded((batch, 4096), 1).cuda()
-    w = seeded((6144 + 64, 4096), 2, 0.02).cuda()     # partial last tile
-    ref = ops.linear(x, w, out_dtype=torch.float32)
-    from llm_compiler_3_b200 import _native
+def test_packed_weights(cuda, batch, packed):
+    """Panels give the bit-identical tensor-core result; at batch 1-2 packed
+    weights run the CUDA-core GEMV, checked against the oracle."""
+    from llm_compiler_3_b200 import _native, ops
+    x = seeded((batch, 4096), 1)
+    w = seeded((6144 + 64, 4096), 2, 0.02)     # partial last tile
+    ref = ops.linear(x.cuda(), w.cuda(), out_dtype=torch.float32)
     e = _native.Epilogue(kind=_native.EPI_STORE, ld_out=w.shape[0], out_f32=1)
     out = torch.empty(batch, w.shape[0], dtype=torch.float32, device="cuda")
     e.out = _p(out)
-    ops.projection(x, ops.pack_weight(w) if packed else w, w.shape[0], e, packed=packed)
-    assert torch.equal(out, ref)
+    wd = w.cuda()
+    ops.projection(x.cuda(), ops.pack_weight(wd) if packed else wd, w.shape[0], e, packed=packed)
+    if packed and batch <= 2:
+        _close(out, oracle.linear(x, w), atol=1e-3)
+    else:
+        assert torch.equal(out, ref)
 
 
-@pytest.mark.parametrize("batch", [1, 16, 64])
+@pytest.mark.parametrize("batch", [1, 2, 16, 64])
 @pytest.mark.parametrize("qk_norm", [False, True])
-def test_qkv_rope_append(cuda, batch, qk_norm):
+@pytest.mark.parametrize("packed", [False, True])
+def test_qkv_rope_append(cuda, batch, qk_norm, packed):
     """QKV projection with the input RMSNorm scale, optional per-head QK-norm,
     RoPE at per-sequence positions and the KV append (exact slot)."""
     from llm_compiler_3_b200 import _native, ops
@@ -58,7 +77,10 @@ def test_qkv_rope_append(cuda, batch, qk_norm):
     h32 = seeded((batch, H), 3).float()
     norm_w = (1 + 0.1 * seeded((H,), 4).float()).half()
     xw = (h32 * norm_w.float()).half()
-    w = seeded(((qh + 2 * kvh) * 128, H), 5, 0.05)
+    wq = seeded((qh * 128, H), 5, 0.05)
+    wk = seeded((kvh * 128, H), 9, 0.05)
+    wv = seeded((kvh * 128, H), 10, 0.05)
+    w = torch.cat([wq, wk, wv])
     qn = (1 + 0.1 * seeded((128,), 6).float()).half() if qk_norm else None
     kn = (1 + 0.1 * seeded((128,), 7).float()).half() if qk_norm else None
     positions = torch.randint(0, max_seq, (batch,), generator=torch.Generator().manual_seed(8),
@@ -78,7 +100,14 @@ def test_qkv_rope_append(cuda, batch, qk_norm):
     e.k_cache, e.v_cache = _p(kc), _p(vc)
     if qk_norm:
         e.q_norm_w, e.k_norm_w = _p(t["qn"]), _p(t["kn"])
-    ops.projection(xw.to(dev), w.to(dev), w.shape[0], e)
+    rows = w.shape[0]
+    if packed:
+        pairs = _native.PACK_HEAD_PAIRS
+        wd = ops.pack_weight_rows([(wq.to(dev), pairs, 0), (wk.to(dev), pairs, qh * 128),
+                                   (wv.to(dev), pairs, (qh + kvh) * 128)], rows)
+    else:
+        wd = _pair_order(w, qh + 2 * kvh).to(dev)
+    ops.projection(xw.to(dev), wd, rows, e, packed=packed)
     # Oracle: RMSNorm(h) with norm_w, linear, QK-norm, RoPE.
     hn = oracle.rms_norm(h32, norm_w, eps)
     proj = oracle.linear(hn, w)
@@ -101,8 +130,10 @@ def test_qkv_rope_append(cuda, batch, qk_norm):
         assert bool((kcpu[b][:, keep] == 7.0).all()) and bool((vcpu[b][:, keep] == 7.0).all())
 
 
-@pytest.mark.parametrize("batch", [1, 16, 64])
-def test_residual_and_next_norm(cuda, batch):
+@pytest.mark.parametrize("batch", [1, 2, 16, 64])
+@pytest.mark.parametrize("rows", [128, 16])
+@pytest.mark.parametrize("packed", [False, True])
+def test_residual_and_next_norm(cuda, batch, rows, packed):
     from llm_compiler_3_b200 import _native, ops
     H, K = 1024, 512
     x = seeded((batch, K), 11)
@@ -112,30 +143,29 @@ def test_residual_and_next_norm(cuda, batch):
     dev = "cuda"
     r_d = resid.clone().to(dev)
     xw = torch.empty(batch, H, dtype=torch.float16, device=dev)
-    ssq = torch.zeros(H // 128, batch, dtype=torch.float32, device=dev)
+    ssq = torch.zeros(H // rows, batch, dtype=torch.float32, device=dev)
     nw = norm_w.to(dev)
-    e = _native.Epilogue(kind=_native.EPI_RESID, ld_resid=H, ld_xw=H, ssq_out_ld=batch)
+    e = _native.Epilogue(kind=_native.EPI_RESID, ld_resid=H, ld_xw=H, ssq_out_ld=batch,
+                         ssq_out_rows=rows)
     e.resid, e.norm_w, e.xw, e.ssq_out = _p(r_d), _p(nw), _p(xw), _p(ssq)
-    ops.projection(x.to(dev), w.to(dev), H, e)
+    wd = ops.pack_weight(w.to(dev)) if packed else w.to(dev)
+    ops.projection(x.to(dev), wd, H, e, packed=packed)
     h = resid + oracle.linear(x, w)
     _close(r_d, h, atol=1e-3)
     _close(xw, h * norm_w.float())
-    ref_ssq = (h * h).view(batch, H // 128, 128).sum(-1).t()
+    ref_ssq = (h * h).view(batch, H // rows, rows).sum(-1).t()
     torch.testing.assert_close(ssq.cpu(), ref_ssq, rtol=1e-4, atol=1e-3)
 
 
-@pytest.mark.parametrize("batch", [1, 16, 64])
-def test_swiglu(cuda, batch):
+@pytest.mark.parametrize("batch", [1, 2, 16, 64])
+@pytest.mark.parametrize("packed", [False, True])
+def test_swiglu(cuda, batch, packed):
     from llm_compiler_3_b200 import _native, ops
     H, F = 512, 384
     h32 = seeded((batch, H), 21).float()
     xw = h32.half()
     gate = seeded((F, H), 22, 0.05)
     up = seeded((F, H), 23, 0.05)
-    w = torch.empty(2 * F, H, dtype=torch.float16)
-    for j in range(F // 64):      # [gate 64 | up 64] per 128-row tile
-        w[128 * j:128 * j + 64] = gate[64 * j:64 * j + 64]
-        w[128 * j + 64:128 * j + 128] = up[64 * j:64 * j + 64]
     ssq = _norm_input(h32, batch)
     dev = "cuda"
     act = torch.empty(batch, F, dtype=torch.float16, device=dev)
@@ -143,26 +173,46 @@ def test_swiglu(cuda, batch):
     e = _native.Epilogue(kind=_native.EPI_SWIGLU, ssq_parts=4, ssq_ld=batch, hidden=H,
                          ssq_eps=1e-5, ld_out=F)
     e.ssq_in, e.out = _p(s_d), _p(act)
-    ops.projection(xw.to(dev), w.to(dev), 2 * F, e)
+    if packed:
+        il = _native.PACK_INTERLEAVE
+        wd = ops.pack_weight_rows([(gate.to(dev), il, 0), (up.to(dev), il, 1)], 2 * F)
+    else:
+        wd = _interleave(gate, up).to(dev)
+    ops.projection(xw.to(dev), wd, 2 * F, e, packed=packed)
     hn = oracle.rms_norm(h32, torch.ones(H), 1e-5)
     ref = oracle.silu_mul(oracle.linear(hn, gate), oracle.linear(hn, up))
     _close(act, ref)
 
 
-@pytest.mark.parametrize("batch", [1, 16, 64])
-def test_argmax_partials(cuda, batch):
+@pytest.mark.parametrize("batch", [1, 2, 16, 64])
+@pytest.mark.parametrize("rows", [128, 16])
+@pytest.mark.parametrize("vocab", [1000, 1008])
+@pytest.mark.parametrize("packed", [False, True])
+def test_argmax_partials(cuda, batch, rows, vocab, packed):
+    """Per-`rows` partial (max, argmax); 1008 rows at batch 1-2 with 16-row
+    partials and packed weights take the GEMV, 1000 the tensor cores."""
     from llm_compiler_3_b200 import _native, ops
-    V, H = 1000, 256
+    V, H = vocab, 256
     x = seeded((batch, H), 31)
     w = seeded((V, H), 32, 0.05)
-    tiles = (V + 127) // 128
+    parts = (V + rows - 1) // rows
     dev = "cuda"
-    val = torch.empty(tiles, batch, dtype=torch.float32, device=dev)
-    idx = torch.empty(tiles, batch, dtype=torch.int32, device=dev)
-    e = _native.Epilogue(kind=_native.EPI_ARGMAX, am_ld=batch)
+    val = torch.full((parts, batch), float("nan"), dtype=torch.float32, device=dev)
+    idx = torch.full((parts, batch), -1, dtype=torch.int32, device=dev)
+    e = _native.Epilogue(kind=_native.EPI_ARGMAX, am_ld=batch, am_rows=rows)
     e.am_val, e.am_idx = _p(val), _p(idx)
-    ops.projection(x.to(dev), w.to(dev), V, e)
+    wd = ops.pack_weight(w.to(dev)) if packed else w.to(dev)
+    ops.projection(x.to(dev), wd, V, e, packed=packed)
     logits = oracle.linear(x, w)
-    best = val.cpu().max(0)
-    got_ids = idx.cpu().gather(0, best.indices[None])[0]
+    val_c, idx_c = val.cpu(), idx.cpu()
+    for p in range(parts):      # every partial is its rows' argmax
+        lo, hi = p * rows, min(V, (p + 1) * rows)
+        ref_v, ref_i = logits[:, lo:hi].max(1)
+        torch.testing.assert_close(val_c[p], ref_v, rtol=0, atol=1e-3)
+        close = (idx_c[p].long() == ref_i + lo) | \
+            ((logits[:, lo:hi].gather(1, (idx_c[p].long() - lo).clamp(0, hi - lo - 1)[:, None])[:, 0]
+              - ref_v).abs() <= 1e-3)
+        assert bool(close.all()) and bool(((idx_c[p] >= lo) & (idx_c[p] < hi)).all())
+    best = val_c.max(0)
+    got_ids = idx_c.gather(0, best.indices[None])[0]
     assert torch.equal(got_ids.long(), oracle.greedy_argmax(logits))
