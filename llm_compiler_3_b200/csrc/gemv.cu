@@ -10,7 +10,8 @@
 // with another CTA: no split-K, no fix-up.  The grid is one wave of persistent
 // CTAs, each walking a balanced share of the groups.  In every CTA one
 // producer warp streams the slices with bulk copies, four panels (8 KB) per
-// ring stage, a ring deep enough to keep ~64 KB in flight per CTA.  Each of
+// ring stage, the ring as deep as shared memory allows (launch_gemv trades
+// CTAs per SM against stages for the most bytes in flight).  Each of
 // four consumer warps takes one panel of a stage: the group's 16 rows are
 // exactly the M of mma.sync m16n8k16 (A fetched with ldmatrix from the
 // swizzled slice, the one or two tokens in N = 8, FP32 accumulators), which
@@ -23,6 +24,8 @@
 // (lib/Transforms/HardwareOps.cpp:105-155, lib/Transforms/Emit.cpp:348-378)
 // with FP16 operands and FP32 accumulation (lib/Transforms/Normalize.cpp:123-192).
 #include <math.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "host.hpp"
@@ -38,7 +41,7 @@ constexpr int kGemvThreads = kConsumers + 32;  // + producer warp 4
 constexpr int kPanelsPerStage = 4;
 constexpr int kSlice = kRows * 128;        // bytes of one group's slice of a panel
 constexpr int kStageBytes = kPanelsPerStage * kSlice;
-constexpr int kGemvStages = 8;
+constexpr int kMaxStages = 16;
 constexpr int kGemvSmemPerSm = 233472;     // usable shared memory per SM
 constexpr int kGemvSmemReserved = 1024;    // per CTA, taken by the runtime
 
@@ -79,13 +82,14 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 template <int BT>
 __global__ void __launch_bounds__(kGemvThreads)
     gemv_kernel(const uint8_t* __restrict__ w_packed, const __half* __restrict__ x,
-                const __grid_constant__ EpiParams ep, int k, int kblocks, int n_groups) {
+                const __grid_constant__ EpiParams ep, int k, int kblocks, int n_groups,
+                int stages) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  __half* xs = reinterpret_cast<__half*>(ring + kGemvStages * kStageBytes);  // [BT][k]
+  __half* xs = reinterpret_cast<__half*>(ring + stages * kStageBytes);  // [BT][k]
   uint64_t* full = reinterpret_cast<uint64_t*>(xs + BT * k);
-  uint64_t* empty = full + kGemvStages;
-  float* part_sum = reinterpret_cast<float*>(empty + kGemvStages);  // [4 warps][16 rows][2]
+  uint64_t* empty = full + kMaxStages;
+  float* part_sum = reinterpret_cast<float*>(empty + kMaxStages);  // [4 warps][16 rows][2]
   float* red = part_sum + 4 * kRows * 2;                        // [4 warps][BT]
   int* red_id = reinterpret_cast<int*>(red + 4 * BT);          // [4 warps][BT]
   float* rn = reinterpret_cast<float*>(red_id + 4 * BT);       // [BT] RMSNorm scale
@@ -97,7 +101,7 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   pdl_launch_dependents();
   if (t == 0) {
-    for (int s = 0; s < kGemvStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers / 32);
     }
@@ -111,29 +115,33 @@ __global__ void __launch_bounds__(kGemvThreads)
     // without waiting for it.
     if (lane != 0) return;
     const uint64_t pol = policy_evict_first();
-    int it = 0;
+    int it = 0, slot = 0;
+    uint32_t phase = 0;  // phase of the current pass over the ring
     bool ok = true;
     for (int g = blockIdx.x; g < n_groups && ok; g += gridDim.x) {
       const int row0 = g * kRows;
       const uint8_t* base =
           w_packed + static_cast<size_t>(row0 >> 7) * kblocks * 16384 + (row0 & 127) * 128;
       for (int ks = 0; ks < kstages; ++ks, ++it) {
-        const int s = it % kGemvStages;
-        if (!wait_or_abort(&empty[s], ((it / kGemvStages) & 1) ^ 1, abort_flag) || *abort_flag) {
+        if (!wait_or_abort(&empty[slot], phase ^ 1, abort_flag) || *abort_flag) {
           ok = false;
           break;
         }
         const int kb0 = ks * kPanelsPerStage;
         const int nk = min(kPanelsPerStage, kblocks - kb0);
-        mbar_arrive_expect_tx(&full[s], nk * kSlice);
+        mbar_arrive_expect_tx(&full[slot], nk * kSlice);
         for (int j = 0; j < nk; ++j)
-          bulk_load_hint(ring + s * kStageBytes + j * kSlice,
-                         base + static_cast<size_t>(kb0 + j) * 16384, kSlice, &full[s], pol);
+          bulk_load_hint(ring + slot * kStageBytes + j * kSlice,
+                         base + static_cast<size_t>(kb0 + j) * 16384, kSlice, &full[slot], pol);
+        if (++slot == stages) {
+          slot = 0;
+          phase ^= 1;
+        }
       }
     }
     if (!ok)  // the CTA may not exit with copies still landing in its ring
-      for (int i = max(0, it - kGemvStages); i < it; ++i)
-        mbar_wait(&full[i % kGemvStages], (i / kGemvStages) & 1, kDevErrTmaTimeout);
+      for (int i = max(0, it - stages); i < it; ++i)
+        mbar_wait(&full[i % stages], (i / stages) & 1, kDevErrTmaTimeout);
     return;
   }
 
@@ -168,19 +176,22 @@ __global__ void __launch_bounds__(kGemvThreads)
   // A fragment is (rows 0-7 | 8-15) x (k 0-7 | 8-15).
   const int a_row = ((lane >> 3) & 1) * 8 + (lane & 7), a_chunk = lane >> 4;
   const int b_tok = lane >> 2, b_k = 2 * (lane & 3);  // B fragment: token, k pair
-  int it = 0;
+  int slot = 0;
+  uint32_t phase = 0;
   for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    // One accumulator per k-step of a panel: four independent MMA chains.
+    float c[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) c[kk][0] = c[kk][1] = c[kk][2] = c[kk][3] = 0.f;
     bool bad = false;
-    for (int ks = 0; ks < kstages; ++ks, ++it) {
-      const int s = it % kGemvStages;
-      if (!bad && !wait_or_abort(&full[s], (it / kGemvStages) & 1, abort_flag)) {
+    for (int ks = 0; ks < kstages; ++ks) {
+      if (!bad && !wait_or_abort(&full[slot], phase, abort_flag)) {
         bad = true;
         *abort_flag = 1;
       }
       const int kb = ks * kPanelsPerStage + warp;  // this warp's panel
       if (!bad && kb < kblocks) {
-        const uint32_t slice = smem_u32(ring + s * kStageBytes + warp * kSlice) + a_row * 128;
+        const uint32_t slice = smem_u32(ring + slot * kStageBytes + warp * kSlice) + a_row * 128;
         const __half* xk = xs + kb * 64 + b_k;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -190,21 +201,28 @@ __global__ void __launch_bounds__(kGemvThreads)
             b0 = *reinterpret_cast<const uint32_t*>(xk + b_tok * k + kk * 16);
             b1 = *reinterpret_cast<const uint32_t*>(xk + b_tok * k + kk * 16 + 8);
           }
-          mma_16816(c, a0, a1, a2, a3, b0, b1);
+          mma_16816(c[kk], a0, a1, a2, a3, b0, b1);
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == stages) {
+        slot = 0;
+        phase ^= 1;
+      }
     }
     if (consumer_sync_or(bad)) return;
 
     // Add the four warps' sums (lanes 4i hold rows i and i + 8, tokens 0-1).
     if ((lane & 3) == 0) {
       float* ps = part_sum + warp * kRows * 2;
-      ps[(lane >> 2) * 2] = c[0];
-      ps[(lane >> 2) * 2 + 1] = c[1];
-      ps[((lane >> 2) + 8) * 2] = c[2];
-      ps[((lane >> 2) + 8) * 2 + 1] = c[3];
+      float v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = (c[0][q] + c[1][q]) + (c[2][q] + c[3][q]);
+      ps[(lane >> 2) * 2] = v[0];
+      ps[(lane >> 2) * 2 + 1] = v[1];
+      ps[((lane >> 2) + 8) * 2] = v[2];
+      ps[((lane >> 2) + 8) * 2 + 1] = v[3];
     }
     consumer_sync();
     float acc[BT];
@@ -342,33 +360,62 @@ __global__ void __launch_bounds__(kGemvThreads)
 }
 
 template <int BT>
-size_t gemv_smem(int k) {
+size_t gemv_smem(int k, int stages) {
   // ring + staged activations + full/empty barriers + reduction scratch
-  return static_cast<size_t>(kGemvStages) * kStageBytes + static_cast<size_t>(BT) * k * 2 +
-         2 * kGemvStages * 8 + (4 * kRows * 2 + 4 * BT + 4 * BT + BT + BT + 1) * 4 + 64;
+  return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(BT) * k * 2 +
+         2 * kMaxStages * 8 + (4 * kRows * 2 + 4 * BT + 4 * BT + BT + BT + 1) * 4 + 64;
+}
+
+struct GemvLaunch {
+  int grid = 0, stages = 0;
+};
+
+// One wave of persistent CTAs.  For 1-4 CTAs per SM take the deepest ring
+// that fits and spread the groups so every CTA walks the same number (+-1);
+// keep the choice with the most bytes in flight up to 12 MB (about where bulk
+// streams saturate HBM), then the most CTAs, then the deepest ring.
+template <int BT>
+GemvLaunch choose_launch(int n_rows, int k) {
+  const int n_groups = n_rows / kRows;
+  const size_t fixed = gemv_smem<BT>(k, 0);
+  GemvLaunch best;
+  long long best_score = -1;
+  for (int per_sm = 1; per_sm <= 4; ++per_sm) {
+    const long long avail = kGemvSmemPerSm / per_sm - kGemvSmemReserved - static_cast<long long>(fixed);
+    const int stages = static_cast<int>(std::min<long long>(kMaxStages, avail / kStageBytes));
+    if (stages < 4) break;
+    const int slots = per_sm * sm_count();
+    const int rounds = (n_groups + slots - 1) / slots;
+    const int grid = (n_groups + rounds - 1) / rounds;
+    const long long score =
+        std::min<long long>(static_cast<long long>(grid) * stages * kStageBytes, 12ll << 20);
+    if (score > best_score || (score == best_score && (grid > best.grid ||
+                                                       (grid == best.grid && stages > best.stages)))) {
+      best_score = score;
+      best.grid = grid;
+      best.stages = stages;
+    }
+  }
+  return best;
 }
 
 template <int BT>
 int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams& ep,
                 cudaStream_t stream, bool pdl) {
-  const size_t smem = gemv_smem<BT>(k);
+  const GemvLaunch g = choose_launch<BT>(n_rows, k);
+  NPU_REQUIRE(g.grid > 0, "gemv: activations of K=%d leave no room for the ring", k);
+  const size_t smem = gemv_smem<BT>(k, g.stages);
   auto kern = gemv_kernel<BT>;
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
-  // One wave of persistent CTAs, as many per SM as shared memory allows, and
-  // the groups spread so that every CTA walks the same number (+-1).
-  const int per_sm = max(1, min(8, kGemvSmemPerSm / static_cast<int>(smem + kGemvSmemReserved)));
-  const int n_groups = n_rows / kRows;
-  const int slots = per_sm * sm_count();
-  const int rounds = (n_groups + slots - 1) / slots;
   LaunchCfg cfg;
-  cfg.grid = dim3((n_groups + rounds - 1) / rounds);
+  cfg.grid = dim3(g.grid);
   cfg.block = dim3(kGemvThreads);
   cfg.smem = smem;
   cfg.stream = stream;
   cfg.pdl = pdl;
   return launch(cfg, kern, static_cast<const uint8_t*>(w), static_cast<const __half*>(x), ep, k,
-                k / 64, n_groups);
+                k / 64, n_rows / kRows, g.stages);
 }
 
 }  // namespace
