@@ -273,7 +273,9 @@ NPU_B200_API int npu_b200_load_plan(npu_b200_ctx* ctx, const char* plan_path);
 NPU_B200_API int npu_b200_plan_check(const char* plan_path, int64_t* out, int n);
 
 /* out[0..11] = layers, hidden, local q heads, local kv heads, local ffn, local vocab,
- * vocab offset, max_batch, max_seq, head_dim, plan fingerprint (FNV-1a), tp_size. */
+ * vocab offset, max_batch, max_seq, head_dim, plan fingerprint (FNV-1a), tp_size;
+ * out[12] (when n >= 13) = 1 if the tensor-parallel all-reduces run over NVLink
+ * peer memory, 0 if through NCCL (NPU_B200_TP_EXCHANGE=nccl, or CUDA IPC unusable). */
 NPU_B200_API int npu_b200_plan_info(const npu_b200_ctx* ctx, int64_t* out, int n);
 
 /* Copy one whole FP16 parameter (host or device memory) into this rank's layout.

@@ -244,7 +244,9 @@ __global__ void __launch_bounds__(kGemvThreads)
             float v = acc[b] + bias;
             if (ep.relu) v = fmaxf(v, 0.f);
             const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
-            if (ep.out_f32)
+            if (ep.px.seq >= 0)
+              px_store(ep.px, px_tag(ep.px, ep.px.seq), b, n, v);
+            else if (ep.out_f32)
               static_cast<float*>(ep.out)[off] = v;
             else
               static_cast<__half*>(ep.out)[off] = __float2half_rn(v);

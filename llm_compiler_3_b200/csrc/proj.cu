@@ -159,7 +159,9 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
           float val = v[q] + bias;
           if (ep.relu) val = fmaxf(val, 0.f);
           const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
-          if (ep.out_f32)
+          if (ep.px.seq >= 0)
+            px_store(ep.px, px_tag(ep.px, ep.px.seq), b, n, val);
+          else if (ep.out_f32)
             static_cast<float*>(ep.out)[off] = val;
           else
             static_cast<__half*>(ep.out)[off] = __float2half_rn(val);
@@ -886,7 +888,13 @@ int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int
   if (ep.kind == kEpiResid)
     NPU_REQUIRE(ep.ssq_out_ld >= batch && (ep.ssq_out_rows == 16 || ep.ssq_out_rows == 128),
                 "projection: sums of squares need ssq_out_ld >= batch and 16 or 128 rows per partial");
-  if (ep.kind == kEpiStore) NPU_REQUIRE(ep.out != nullptr, "projection: null output");
+  if (ep.kind == kEpiStore)
+    NPU_REQUIRE(ep.out != nullptr || ep.px.seq >= 0, "projection: null output");
+  if (ep.px.seq >= 0)
+    NPU_REQUIRE(ep.kind == kEpiStore && ep.px.ranks >= 1 && ep.px.ranks <= kMaxRanks &&
+                    ep.px.seq < kArgmaxSeq && ep.n_rows == ep.px.hidden &&
+                    batch <= ep.px.max_batch && ep.px.epoch,
+                "projection: peer exchange needs a STORE of all hidden rows");
   NPU_REQUIRE(ep.kind >= kEpiStore && ep.kind <= kEpiArgmax, "projection: unknown epilogue %d",
               ep.kind);
   NPU_REQUIRE(ep.ssq_in == nullptr || (ep.ssq_parts >= 1 && ep.ssq_ld >= batch),

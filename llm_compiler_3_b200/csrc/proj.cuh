@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "peer.cuh"
+
 namespace npu_b200 {
 
 // What the epilogue does with the FP32 tile (128 weight rows x up to BN tokens).
@@ -66,6 +68,10 @@ struct EpiParams {
   int32_t* am_idx = nullptr;
   int am_ld = 0;
   int am_rows = 128;          // rows per partial (max, argmax): 128 or 16
+
+  // kEpiStore with px.seq >= 0: instead of `out`, store the FP32 value in this
+  // rank's exchange buffer and raise the row-group flags on every rank (peer.cuh).
+  PeerExchange px;
 };
 
 // Runs the projection.  w is [n_rows, k] FP16 row-major, or (w_packed) the

@@ -292,6 +292,13 @@ struct npu_b200_ctx {
   __half* h_hidden = nullptr;
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (mode, batch)
   std::vector<uint8_t> have;                              // [layers * kPerLayerKinds + 3]
+  // Tensor parallel over NVLink peer memory (peer.cuh): this rank's exchange
+  // buffer, the peers' opened through CUDA IPC, the step counter.
+  uint32_t* epoch = nullptr;
+  uint64_t* px_part = nullptr;
+  std::vector<void*> px_opened;  // peers' IPC mappings, closed before the local buffers are freed
+  bool px_ready = false;         // false: the all-reduces go through NCCL
+  PeerExchange px;               // seq filled in per exchange
 };
 
 namespace npu_b200 {
@@ -328,12 +335,87 @@ int halloc(npu_b200_ctx* c, size_t count, T** out) {
 void release(npu_b200_ctx* c) {
   for (auto& g : c->graphs) cudaGraphExecDestroy(g.second);
   c->graphs.clear();
+  for (void* p : c->px_opened) cudaIpcCloseMemHandle(p);
+  c->px_opened.clear();
+  c->px_ready = false;
   for (void* p : c->device_allocs) cudaFree(p);
   c->device_allocs.clear();
   for (void* p : c->host_allocs) cudaFreeHost(p);
   c->host_allocs.clear();
   c->layers.clear();
   c->loaded = false;
+}
+
+// Opens every rank's exchange buffers through CUDA IPC (handles all-gathered
+// over NCCL, a collective of all ranks).  If this machine does not allow it, or
+// NPU_B200_TP_EXCHANGE=nccl, the all-reduces stay on NCCL; every rank must take
+// the same path, so the ranks agree on it with one more all-reduce.
+int setup_peer_exchange(npu_b200_ctx* c) {
+  const Plan& P = c->plan;
+  const int T = c->tp_size;
+  NPU_REQUIRE(T <= kMaxRanks, "tensor parallel: at most %d ranks", kMaxRanks);
+  const size_t B = static_cast<size_t>(P.max_batch), H = static_cast<size_t>(P.hidden);
+  const size_t part_words = 2 * B * H + B * 2;
+  int rc = 0;
+  if ((rc = dalloc(c, part_words, &c->px_part))) return rc;
+  const char* env = getenv("NPU_B200_TP_EXCHANGE");
+  int usable = !(env && strcmp(env, "nccl") == 0);
+  cudaIpcMemHandle_t mine;
+  memset(&mine, 0, sizeof(mine));
+  if (usable && cudaIpcGetMemHandle(&mine, c->px_part) != cudaSuccess) {
+    cudaGetLastError();
+    usable = 0;
+  }
+  // Every rank's handle, and a vote (minimum over ranks) on whether to use them.
+  const size_t hbytes = sizeof(cudaIpcMemHandle_t);
+  uint8_t* d_all = nullptr;
+  int32_t* d_vote = nullptr;
+  if ((rc = dalloc(c, hbytes * T, &d_all)) || (rc = dalloc(c, 1, &d_vote))) return rc;
+  NPU_TRY_CUDA(cudaMemcpy(d_all + hbytes * c->tp_rank, &mine, hbytes, cudaMemcpyHostToDevice));
+  NPU_TRY_CUDA(cudaMemcpy(d_vote, &usable, sizeof(int32_t), cudaMemcpyHostToDevice));
+  if ((rc = check_nccl(g_nccl.AllGather(d_all + hbytes * c->tp_rank, d_all, hbytes, ncclUint8,
+                                        c->comm, c->stream),
+                       "ncclAllGather(ipc handles)")) ||
+      (rc = check_nccl(g_nccl.AllReduce(d_vote, d_vote, 1, ncclInt32, ncclMin, c->comm, c->stream),
+                       "ncclAllReduce(peer exchange vote)")))
+    return rc;
+  NPU_TRY_CUDA(cudaStreamSynchronize(c->stream));
+  std::vector<uint8_t> all(hbytes * T);
+  int32_t agreed = 0;
+  NPU_TRY_CUDA(cudaMemcpy(all.data(), d_all, all.size(), cudaMemcpyDeviceToHost));
+  NPU_TRY_CUDA(cudaMemcpy(&agreed, d_vote, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  PeerExchange& x = c->px;
+  x.rank = c->tp_rank;
+  x.ranks = T;
+  x.max_batch = P.max_batch;
+  x.hidden = P.hidden;
+  x.epoch = c->epoch;
+  int opened_ok = agreed;
+  for (int r = 0; r < T && opened_ok; ++r) {
+    if (r == c->tp_rank) {
+      x.part[r] = c->px_part;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, all.data() + hbytes * r, sizeof(h));
+    void* pr = nullptr;
+    if (cudaIpcOpenMemHandle(&pr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      opened_ok = 0;
+      break;
+    }
+    c->px_opened.push_back(pr);
+    x.part[r] = static_cast<uint64_t*>(pr);
+  }
+  // Every rank must have opened every peer before anyone relies on it.
+  NPU_TRY_CUDA(cudaMemcpy(d_vote, &opened_ok, sizeof(int32_t), cudaMemcpyHostToDevice));
+  if ((rc = check_nccl(g_nccl.AllReduce(d_vote, d_vote, 1, ncclInt32, ncclMin, c->comm, c->stream),
+                       "ncclAllReduce(peer exchange vote)")))
+    return rc;
+  NPU_TRY_CUDA(cudaStreamSynchronize(c->stream));
+  NPU_TRY_CUDA(cudaMemcpy(&agreed, d_vote, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  c->px_ready = agreed != 0;
+  return NPU_B200_OK;
 }
 
 int allocate(npu_b200_ctx* c) {
@@ -417,6 +499,8 @@ int allocate(npu_b200_ctx* c) {
       (rc = halloc(c, B, &c->h_ids)) || (rc = halloc(c, B * H, &c->h_hidden)))
     return rc;
   c->have.assign(static_cast<size_t>(P.layers) * kPerLayerKinds + 3, 0);
+  if ((rc = dalloc(c, 1, &c->epoch))) return rc;
+  if (T > 1 && (rc = setup_peer_exchange(c))) return rc;
   return NPU_B200_OK;
 }
 
@@ -607,8 +691,11 @@ void norm_input(const npu_b200_ctx* c, int batch, EpiParams* e) {
   e->ssq_eps = c->plan.eps;
 }
 
+// The projection that closes a sub-block (o_proj / down_proj): residual add
+// and the next RMSNorm's input; with tensor parallelism first the sum of the
+// ranks' partials (exchange `seq` of the step: 2 per layer).
 int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int batch,
-                 const __half* next_norm, cudaStream_t s) {
+                 const __half* next_norm, int seq, cudaStream_t s) {
   const Plan& P = c->plan;
   EpiParams e;
   e.n_rows = P.hidden;
@@ -629,14 +716,23 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
   e.out = c->partial;
   e.ld_out = P.hidden;
   e.out_f32 = 1;
+  if (c->px_ready) {  // tagged partials into this rank's exchange buffer
+    e.px = c->px;
+    e.px.seq = seq;
+  }
   int rc = proj_run(w, true, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
   if (rc) return rc;
-  if ((rc = check_nccl(g_nccl.AllReduce(c->partial, c->partial,
+  if (!c->px_ready &&
+      (rc = check_nccl(g_nccl.AllReduce(c->partial, c->partial,
                                         static_cast<size_t>(batch) * P.hidden, ncclFloat32,
                                         ncclSum, c->comm, s),
                        "ncclAllReduce")))
     return rc;
   ResidualUpdate u;
+  if (c->px_ready) {
+    u.px = c->px;
+    u.px.seq = seq;
+  }
   u.mode = kResidAddPartial;
   u.batch = batch;
   u.hidden = P.hidden;
@@ -647,7 +743,7 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
   u.ssq_out = c->ssq;
   u.ssq_ld = P.max_batch;
   u.ssq_rows = part_rows(batch);
-  return residual_update(u, s, false);
+  return residual_update(u, s, c->px_ready);  // PDL only after our own kernel, not NCCL
 }
 
 int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
@@ -673,6 +769,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
     u.seq_lens = c->d_seq_lens;
     u.inv_freq = c->d_inv_freq;
     u.rope_tab = c->rope_tab;
+    u.epoch = c->epoch;
     if ((rc = residual_update(u, s, true))) return rc;
   }
   for (int l = 0; l < P.layers; ++l) {
@@ -703,7 +800,8 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
                                c->q_loc, c->kv_loc, D, P.max_seq, 1.f / sqrtf(static_cast<float>(D)),
                                0, c->fd_ws, c->fd_ws_bytes, s, true)))
       return rc;
-    if ((rc = residual_out(c, L.w_o, c->attn, c->q_loc * D, batch, L.post_norm, s))) return rc;
+    if ((rc = residual_out(c, L.w_o, c->attn, c->q_loc * D, batch, L.post_norm, 2 * l, s)))
+      return rc;
     EpiParams g;
     g.kind = kEpiSwiGLU;
     g.n_rows = 2 * c->ffn_loc;
@@ -716,7 +814,8 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
       return rc;
     const __half* next = l + 1 < P.layers ? c->layers[l + 1].in_norm
                                           : (c->final_norm ? c->final_norm : L.in_norm);
-    if ((rc = residual_out(c, L.w_down, c->act, c->ffn_loc, batch, next, s))) return rc;
+    if ((rc = residual_out(c, L.w_down, c->act, c->ffn_loc, batch, next, 2 * l + 1, s)))
+      return rc;
   }
   if (mode == kModeHidden)
     return store_hidden(c->resid, c->hidden_io, static_cast<size_t>(batch) * H, s, true);
@@ -737,6 +836,14 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
   if (c->tp_size == 1)
     return argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
                          c->gather_send, c->d_ids, s, true);
+  if (c->px_ready) {
+    PeerExchange x = c->px;
+    x.seq = kArgmaxSeq;
+    if ((rc = argmax_reduce_push(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch,
+                                 c->vocab_off, x, s, true)))
+      return rc;
+    return argmax_combine_peers(x, batch, c->d_ids, s, true);
+  }
   if ((rc = argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
                           c->gather_send, reinterpret_cast<int32_t*>(c->gather_send + P.max_batch),
                           s, true)))
@@ -887,11 +994,11 @@ extern "C" int npu_b200_plan_info(const npu_b200_ctx* c, int64_t* out, int n) {
   clear_error();
   NPU_REQUIRE(c && out && n >= 12, "plan_info needs a context and 12 slots");
   if (!c->loaded) return set_error(NPU_B200_E_STATE, "no plan loaded");
-  const int64_t v[12] = {c->plan.layers, c->plan.hidden, c->q_loc, c->kv_loc, c->ffn_loc,
+  const int64_t v[13] = {c->plan.layers, c->plan.hidden, c->q_loc, c->kv_loc, c->ffn_loc,
                          c->vocab_loc, c->vocab_off, c->plan.max_batch, c->plan.max_seq,
                          c->plan.head_dim, static_cast<int64_t>(c->plan.fingerprint & 0x7fffffffffffffffll),
-                         c->tp_size};
-  for (int i = 0; i < 12; ++i) out[i] = v[i];
+                         c->tp_size, c->px_ready ? 1 : 0};
+  for (int i = 0; i < (n < 13 ? n : 13); ++i) out[i] = v[i];
   return NPU_B200_OK;
 }
 

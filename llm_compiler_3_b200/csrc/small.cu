@@ -7,7 +7,9 @@
 //    projection turns into the RMSNorm scale in its epilogue
 //    (lib/Transforms/Pipeline.cpp:149-185: row reductions in FP32).
 //  * argmax_reduce / argmax_combine: greedy token choice over the per-tile
-//    (max, index) pairs the LM-head epilogue leaves, ties to the lowest id.
+//    (max, index) pairs the LM-head epilogue leaves, ties to the lowest id;
+//    with tensor parallelism the per-rank results go through NCCL or, over
+//    peer memory, argmax_reduce_push / argmax_combine_peers.
 //  * store_hidden: FP32 residual -> FP16 hidden-state output.
 #include <math.h>
 
@@ -32,6 +34,7 @@ __global__ void __launch_bounds__(kChunk)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (blockIdx.x == 0 && b == 0 && p.positions && p.seq_lens)
     for (int i = threadIdx.x; i < p.batch; i += blockDim.x) p.seq_lens[i] = p.positions[i] + 1;
+  if (blockIdx.x == 0 && b == 0 && threadIdx.x == 0 && p.epoch) *p.epoch += 1;
   // This step's RoPE angles, once for every layer: theta = float(pos) * inv_freq
   // in FP32 (as transformers forms them), then an accurate sincos.
   if (blockIdx.x == 0 && p.rope_tab && p.positions && threadIdx.x < 64) {
@@ -50,9 +53,23 @@ __global__ void __launch_bounds__(kChunk)
     }
   } else if (p.mode == kResidFromHidden) {
     h = __half2float(p.hidden_in[static_cast<size_t>(b) * p.hidden + n]);
-  } else {
+  } else if (p.px.seq < 0) {
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] +
         p.partial[static_cast<size_t>(b) * p.hidden + n];
+  } else {
+    // Every rank's partial (tagged words, re-read until they have landed),
+    // added in rank order: the same bits on every rank.
+    const uint32_t tag = px_tag(p.px, p.px.seq);
+    float part[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      part[r] = 0.f;
+      if (r < p.px.ranks) px_load(p.px, tag, r, b, n, &part[r]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) sum += part[r];
+    h = p.resid[static_cast<size_t>(b) * p.hidden + n] + sum;
   }
   const float w = __half2float(p.norm_w[n]);
   p.resid[static_cast<size_t>(b) * p.hidden + n] = h;
@@ -126,6 +143,78 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+__global__ void __launch_bounds__(256)
+    argmax_push_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
+                       int n_tiles, int ld, int id_offset, const PeerExchange px) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
+    const float v = part_val[static_cast<size_t>(t) * ld + b];
+    const int i = part_idx[static_cast<size_t>(t) * ld + b];
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    const uint32_t tag = px_tag(px, kArgmaxSeq);
+    uint64_t* w = px.part[px.rank] + px_argmax_offset(px, b);
+    px_put(w, tag, __float_as_uint(bv));
+    px_put(w + 1, tag, static_cast<uint32_t>(bi + id_offset));
+  }
+}
+
+__global__ void argmax_combine_peers_kernel(const PeerExchange px, int batch,
+                                            int32_t* __restrict__ out_ids) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) {
+    const uint32_t tag = px_tag(px, kArgmaxSeq);
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    bool ok = true;
+    for (int r = 0; r < px.ranks && ok; ++r) {
+      const uint64_t* w = px.part[r] + px_argmax_offset(px, b);
+      uint32_t vb = 0, ib = 0;
+      ok = px_get(w, tag, &vb) && px_get(w + 1, tag, &ib);
+      if (!ok) break;
+      const float v = __uint_as_float(vb);
+      const int i = static_cast<int>(ib);
+      if (better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+    out_ids[b] = ok ? bi : -1;
+  }
+}
+
 // gathered: [ranks][2][ld] as {values; ids} per rank.
 __global__ void argmax_combine_kernel(const float* __restrict__ gathered, int ranks, int ld,
                                       int batch, int32_t* __restrict__ out_ids) {
@@ -178,6 +267,29 @@ int argmax_reduce(const float* part_val, const int32_t* part_idx, int n_tiles, i
   cfg.pdl = pdl;
   return launch(cfg, argmax_reduce_kernel, part_val, part_idx, n_tiles, ld, id_offset, out_val,
                 out_idx);
+}
+
+int argmax_reduce_push(const float* part_val, const int32_t* part_idx, int n_tiles, int ld,
+                       int batch, int id_offset, const PeerExchange& px, cudaStream_t stream,
+                       bool pdl) {
+  NPU_REQUIRE(px.ranks >= 1 && px.ranks <= kMaxRanks && batch <= px.max_batch,
+              "argmax: bad peer exchange");
+  LaunchCfg cfg;
+  cfg.grid = dim3(batch);
+  cfg.block = dim3(256);
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, argmax_push_kernel, part_val, part_idx, n_tiles, ld, id_offset, px);
+}
+
+int argmax_combine_peers(const PeerExchange& px, int batch, int32_t* out_ids, cudaStream_t stream,
+                         bool pdl) {
+  LaunchCfg cfg;
+  cfg.grid = dim3((batch + 127) / 128);
+  cfg.block = dim3(128);
+  cfg.stream = stream;
+  cfg.pdl = pdl;
+  return launch(cfg, argmax_combine_peers_kernel, px, batch, out_ids);
 }
 
 int argmax_combine(const float* gathered, int ranks, int ld, int batch, int32_t* out_ids,

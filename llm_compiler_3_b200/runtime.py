@@ -19,7 +19,7 @@ from . import _native
 from .plan import DecodePlan
 
 INFO_FIELDS = ("layers", "hidden", "q_heads", "kv_heads", "ffn", "vocab", "vocab_offset",
-               "max_batch", "max_seq", "head_dim", "fingerprint", "tp_size")
+               "max_batch", "max_seq", "head_dim", "fingerprint", "tp_size", "peer_exchange")
 
 
 class _DeviceArray:
@@ -56,8 +56,8 @@ class Decoder:
         self.info = self._info()
 
     def _info(self) -> dict:
-        out = (ctypes.c_int64 * 12)()
-        _native.check(self.lib.npu_b200_plan_info(self._ctx, out, 12))
+        out = (ctypes.c_int64 * len(INFO_FIELDS))()
+        _native.check(self.lib.npu_b200_plan_info(self._ctx, out, len(INFO_FIELDS)))
         return dict(zip(INFO_FIELDS, list(out)))
 
     # -- weights -----------------------------------------------------------

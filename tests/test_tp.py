@@ -53,7 +53,8 @@ def _weights():
     return top, layers, caches, tokens
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, batch, exchange):
+    os.environ["NPU_B200_TP_EXCHANGE"] = exchange
     import torch.distributed as dist
     from llm_compiler_3_b200.plan import DecodePlan
     from llm_compiler_3_b200.runtime import Decoder, nccl_unique_id
@@ -69,6 +70,7 @@ def _rank_main(rank, world, port, out_dir):
     top, layers, caches, tokens = _weights()
     kv_loc = s.kv_heads // world
     with Decoder(plan, device=rank, tp_rank=rank, tp_size=world, nccl_id=box[0]) as dec:
+        np.save(os.path.join(out_dir, f"peer_r{rank}.npy"), np.array(dec.info["peer_exchange"]))
         for name, t in top.items():
             dec.set_weight(name, t)
         for i, w in enumerate(layers):
@@ -79,7 +81,7 @@ def _rank_main(rank, world, port, out_dir):
                 k, v = dec.kv_cache(i)
                 k.copy_(kc[:, rank * kv_loc:(rank + 1) * kv_loc].cuda())
                 v.copy_(vc[:, rank * kv_loc:(rank + 1) * kv_loc].cuda())
-            ids = dec.step(tokens.numpy(), POSITIONS)
+            ids = dec.step(tokens[:batch].numpy(), POSITIONS[:batch])
             np.save(os.path.join(out_dir, f"ids_r{rank}_s{step}.npy"), ids)
     dist.barrier()
     dist.destroy_process_group()
@@ -92,20 +94,27 @@ def _free_port():
 
 
 @pytest.mark.parametrize("world", [2, 4])
-def test_tensor_parallel_matches_oracle(world):
+@pytest.mark.parametrize("batch", [1, 4])
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_tensor_parallel_matches_oracle(world, batch, exchange):
+    """Batch 1 runs the GEMV projections, batch 4 the tensor-core ones; the
+    all-reduces go over NVLink peer memory (or NCCL when asked)."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"tensor parallel over {world} ranks needs {world} GPUs")
     with tempfile.TemporaryDirectory() as out:
-        mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world,
-                           start_method="spawn", join=True)
+        mp.start_processes(_rank_main, args=(world, _free_port(), out, batch, exchange),
+                           nprocs=world, start_method="spawn", join=True)
         got = [[np.load(os.path.join(out, f"ids_r{r}_s{s}.npy")) for r in range(world)]
                for s in range(2)]
+        peer = [int(np.load(os.path.join(out, f"peer_r{r}.npy"))) for r in range(world)]
+    assert peer == [1 if exchange == "peer" else 0] * world
     top, layers, caches, tokens = _weights()
     ref_ids, logits = oracle.stack_decode(
         lambda i: layers[i], SHAPE.layers, top["model.embed_tokens.weight"],
-        top["model.norm.weight"], top["lm_head.weight"], tokens,
-        torch.tensor(POSITIONS, dtype=torch.int32),
-        lambda i: (caches[i][0].clone(), caches[i][1].clone()), SHAPE, return_logits=True)
+        top["model.norm.weight"], top["lm_head.weight"], tokens[:batch],
+        torch.tensor(POSITIONS[:batch], dtype=torch.int32),
+        lambda i: (caches[i][0][:batch].clone(), caches[i][1][:batch].clone()), SHAPE,
+        return_logits=True)
     from test_decode import _check_ids
     for per_step in got:
         for ids in per_step:
