@@ -1,0 +1,150 @@
+"""Fixed workloads for profiling and timing one kernel or one decode step.
+
+Each case builds seeded synthetic inputs on cuda:0, runs the library's own
+entry point `--repeat` times and prints one line with the mean time of the
+launches after the first (CUDA events).  Under ncu, capture with `-s 1` or
+more to skip the cold first launch.
+
+    python -m llm_compiler_3_b200.cases proj --rows 4096 --k 14336 --batch 1
+    python -m llm_compiler_3_b200.cases flash --batch 64 --seq 4096
+    python -m llm_compiler_3_b200.cases step --batch 1 --layers 32 --seq 4096
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+
+def _timed(fn, repeat: int, graph: bool = False) -> float:
+    """Mean microseconds per call after a first untimed call; with `graph`,
+    the calls are captured once into a CUDA graph and the replay is timed
+    (no host launch cost between kernels)."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    n = max(1, repeat - 1)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(n):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        start.record()
+        g.replay()
+        end.record()
+    else:
+        start.record()
+        for _ in range(n):
+            fn()
+        end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) * 1e3 / n
+
+
+def case_proj(a) -> str:
+    """One packed projection (STORE, FP32 out): the GEMV at batch 1-2, the
+    tensor-core kernel above."""
+    import torch
+    from . import _native, ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = ops.pack_weight((torch.randn(a.rows, a.k, device=dev, generator=g) * 0.02).half())
+    x = torch.randn(a.batch, a.k, device=dev, generator=g).half()
+    out = torch.empty(a.batch, a.rows, device=dev, dtype=torch.float32)
+    e = _native.Epilogue(kind=_native.EPI_STORE, ld_out=a.rows, out_f32=1)
+    e.out = out.data_ptr()
+    us = _timed(lambda: ops.projection(x, w, a.rows, e, packed=True), a.repeat, a.graph)
+    gbs = a.rows * a.k * 2 / us / 1e3
+    return f"proj rows={a.rows} k={a.k} batch={a.batch}: {us:.1f} us/launch, {gbs:.0f} GB/s weights"
+
+
+def case_flash(a) -> str:
+    """Flash-decoding over a full cache of `seq` keys for every sequence."""
+    import torch
+    from . import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(a.batch, a.q_heads, 128, device=dev, generator=g).half()
+    k = torch.randn(a.batch, a.kv_heads, a.seq, 128, device=dev, generator=g).half()
+    v = torch.randn(a.batch, a.kv_heads, a.seq, 128, device=dev, generator=g).half()
+    lens = torch.full((a.batch,), a.seq, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    us = _timed(lambda: ops.flash_decode(q, k, v, lens, out=out), a.repeat, a.graph)
+    gbs = 2 * a.batch * a.kv_heads * a.seq * 128 * 2 / us / 1e3
+    return f"flash batch={a.batch} seq={a.seq}: {us:.1f} us/launch, {gbs:.0f} GB/s K+V"
+
+
+def case_step(a) -> str:
+    """Greedy decode steps of the Llama-3-8B-shaped stack (random weights,
+    cache filled to seq - 1, position seq - 1), one CUDA graph per step."""
+    import torch
+    from . import _native
+    from .plan import llama3_8b
+    from .runtime import Decoder
+    H, V, F = 4096, 128256, 14336
+    dev = torch.device("cuda", 0)
+    dec = Decoder(llama3_8b(layers=a.layers, max_batch=a.batch, max_seq=a.seq), device=0)
+    gen = torch.Generator(device=dev)
+
+    def randn(shape, seed, std=0.02):
+        gen.manual_seed(seed)
+        return (torch.randn(shape, device=dev, generator=gen) * std).half()
+
+    dec.set_weight("model.embed_tokens.weight", randn((V, H), 11))
+    dec.set_weight("lm_head.weight", randn((V, H), 12))
+    ones = torch.ones(H, dtype=torch.float16, device=dev)
+    dec.set_weight("model.norm.weight", ones)
+    shapes = {"self_attn.q_proj.weight": (4096, H), "self_attn.k_proj.weight": (1024, H),
+              "self_attn.v_proj.weight": (1024, H), "self_attn.o_proj.weight": (H, 4096),
+              "mlp.gate_proj.weight": (F, H), "mlp.up_proj.weight": (F, H),
+              "mlp.down_proj.weight": (H, F)}
+    for layer in range(a.layers):
+        for j, (name, shape) in enumerate(shapes.items()):
+            dec.set_weight(f"model.layers.{layer}.{name}", randn(shape, 1000 + 16 * layer + j))
+        dec.set_weight(f"model.layers.{layer}.input_layernorm.weight", ones)
+        dec.set_weight(f"model.layers.{layer}.post_attention_layernorm.weight", ones)
+        k, v = dec.kv_cache(layer)
+        gen.manual_seed(50000 + layer)
+        k[:, :, :a.seq - 1].normal_(generator=gen)
+        v[:, :, :a.seq - 1].normal_(generator=gen)
+    tok = torch.randint(0, V, (a.batch,), device=dev, dtype=torch.int32,
+                        generator=torch.Generator(device=dev).manual_seed(7))
+    pos = torch.full((a.batch,), a.seq - 1, dtype=torch.int32, device=dev)
+    ids = torch.empty(a.batch, dtype=torch.int32, device=dev)
+    us = _timed(lambda: dec.step_device(tok, pos, ids), a.repeat)
+    status = _native.device_status()
+    dec.close()
+    return (f"step batch={a.batch} layers={a.layers} seq={a.seq}: {us / 1e3:.3f} ms/step, "
+            f"device status {status}")
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    sub = ap.add_subparsers(dest="case", required=True)
+    p = sub.add_parser("proj")
+    p.add_argument("--rows", type=int, default=4096)
+    p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--repeat", type=int, default=4)
+    p.add_argument("--graph", action="store_true", help="time graph replays of the launches")
+    f = sub.add_parser("flash")
+    f.add_argument("--batch", type=int, default=64)
+    f.add_argument("--q-heads", type=int, default=32)
+    f.add_argument("--kv-heads", type=int, default=8)
+    f.add_argument("--seq", type=int, default=4096)
+    f.add_argument("--repeat", type=int, default=3)
+    f.add_argument("--graph", action="store_true", help="time graph replays of the launches")
+    s = sub.add_parser("step")
+    s.add_argument("--batch", type=int, default=1)
+    s.add_argument("--layers", type=int, default=32)
+    s.add_argument("--seq", type=int, default=4096)
+    s.add_argument("--repeat", type=int, default=5)
+    a = ap.parse_args(argv)
+    print({"proj": case_proj, "flash": case_flash, "step": case_step}[a.case](a), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -71,10 +71,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   uint8_t* my_stages = smem + warp * STAGES * S::kStageBytes;
   uint64_t* my_bars = bars + warp * STAGES;
+  uint64_t* merge_bar = bars + WARPS * STAGES;  // bulk copy of the split partials
   if (lane == 0) {
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
     for (int s = 0; s < STAGES; ++s) mbar_init(&my_bars[s], 1);
+    if (warp == 0) mbar_init(merge_bar, 1);
     fence_barrier_init();
   }
   __syncwarp();
@@ -329,42 +331,65 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // Merge without serial L2 round trips: all (split, head) statistics are
-  // fetched at once, weights are formed per head, then each thread sums one
-  // 4-dim slice over the splits with independent loads.
+  // Merge without serial L2 round trips.  The splits' outputs (group x D
+  // floats each) come into the idle stage buffers with one bulk copy per split
+  // when they fit, all in flight together; the statistics are fetched at
+  // once; one warp per head forms the split weights with lane-parallel
+  // reductions; then each thread sums one 4-dim slice over the splits.
   const float* up = part + unit * num_splits * S::kPartFloats;
-  float* sw = reinterpret_cast<float*>(smem);      // [num_splits][8] m, then weights
-  float* sl = sw + num_splits * kMaxGroup;         // [num_splits][8] l
-  float* sL = sl + num_splits * kMaxGroup;         // [8] merged row sums
+  const int slab = group * D;  // floats of one split's outputs
+  const bool staged = static_cast<size_t>(num_splits) * slab * 4 + 2 * num_splits * kMaxGroup * 4 +
+                          64 <= static_cast<size_t>(WARPS) * STAGES * S::kStageBytes;
+  float* po = reinterpret_cast<float*>(smem);                   // [num_splits][slab] if staged
+  float* sw = staged ? po + num_splits * slab : po;             // [num_splits][8] m, then weights
+  float* sl = sw + num_splits * kMaxGroup;                      // [num_splits][8] l
+  float* sL = sl + num_splits * kMaxGroup;                      // [8] merged row sums
+  if (staged && threadIdx.x == 0) {
+    // The partials were written by other CTAs' generic stores, and the stage
+    // buffers were last used by this CTA's generic accesses: order both before
+    // this thread's bulk (async-proxy) copies.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(merge_bar, static_cast<uint32_t>(num_splits * slab * 4));
+    const uint64_t pol = policy_evict_first();
+    for (int sp = 0; sp < num_splits; ++sp)
+      bulk_load_hint(po + sp * slab, up + sp * S::kPartFloats, slab * 4, merge_bar, pol);
+  }
   for (int i = threadIdx.x; i < num_splits * group; i += WARPS * 32) {
-    const int s = i / group, head = i - s * group;
-    const float* ps = up + s * S::kPartFloats + kMaxGroup * D;
-    sw[s * kMaxGroup + head] = __ldcg(ps + head);
-    sl[s * kMaxGroup + head] = __ldcg(ps + kMaxGroup + head);
+    const int sp = i / group, head = i - sp * group;
+    const float* ps = up + sp * S::kPartFloats + kMaxGroup * D;
+    sw[sp * kMaxGroup + head] = __ldcg(ps + head);
+    sl[sp * kMaxGroup + head] = __ldcg(ps + kMaxGroup + head);
   }
   __syncthreads();
-  if (threadIdx.x < group) {
-    const int head = threadIdx.x;
+  for (int head = warp; head < group; head += WARPS) {
     float mx = -INFINITY;
-    for (int s = 0; s < num_splits; ++s) mx = fmaxf(mx, sw[s * kMaxGroup + head]);
+    for (int sp = lane; sp < num_splits; sp += 32) mx = fmaxf(mx, sw[sp * kMaxGroup + head]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float L = 0.f;
-    for (int s = 0; s < num_splits; ++s) {
-      const float ms = sw[s * kMaxGroup + head];
+    for (int sp = lane; sp < num_splits; sp += 32) {
+      const float ms = sw[sp * kMaxGroup + head];
       const float wt = ms == -INFINITY ? 0.f : fast_exp2(ms - mx);
-      sw[s * kMaxGroup + head] = wt;
-      L += sl[s * kMaxGroup + head] * wt;
+      sw[sp * kMaxGroup + head] = wt;
+      L += sl[sp * kMaxGroup + head] * wt;
     }
-    sL[head] = L;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) sL[head] = L;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < group * D / 4; idx += WARPS * 32) {
+  bool ready = true;
+  if (staged) ready = mbar_wait(merge_bar, 0, kDevErrTmaTimeout);
+  for (int idx = threadIdx.x; ready && idx < group * D / 4; idx += WARPS * 32) {
     const int head = (idx * 4) / D, dim = idx * 4 - head * D;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
-    for (int s = 0; s < num_splits; ++s) {
-      const float wt = sw[s * kMaxGroup + head];
+    for (int sp = 0; sp < num_splits; ++sp) {
+      const float wt = sw[sp * kMaxGroup + head];
       const float4 pv =
-          __ldcg(reinterpret_cast<const float4*>(up + s * S::kPartFloats + head * D + dim));
+          staged ? *reinterpret_cast<const float4*>(po + sp * slab + head * D + dim)
+                 : __ldcg(reinterpret_cast<const float4*>(up + sp * S::kPartFloats + head * D + dim));
       acc.x += wt * pv.x;
       acc.y += wt * pv.y;
       acc.z += wt * pv.z;
@@ -386,7 +411,7 @@ constexpr int kStages = 3;
 template <int D>
 constexpr size_t fd_smem_bytes() {
   return 1024 + static_cast<size_t>(kWarps) * kStages * FdShape<D>::kStageBytes +
-         kWarps * kStages * sizeof(uint64_t);
+         (kWarps * kStages + 1) * sizeof(uint64_t);
 }
 
 // Splits per (sequence, KV head): the count whose waves of CTAs finish first,

@@ -83,21 +83,41 @@ template <int BT>
 __global__ void __launch_bounds__(kGemvThreads)
     gemv_kernel(const uint8_t* __restrict__ w_packed, const __half* __restrict__ x,
                 const __grid_constant__ EpiParams ep, int k, int kblocks, int n_groups,
-                int stages) {
+                int stages, int split) {
+  // split == 1: persistent CTAs walking groups blockIdx.x, + gridDim.x, ...
+  // split > 1: a cluster of `split` CTAs per group, member r taking the r-th
+  // share of the K stages; the members' sums meet in member 0's shared memory.
+  const int kstages_all = (kblocks + kPanelsPerStage - 1) / kPanelsPerStage;
+  const int crank = split > 1 ? static_cast<int>(blockIdx.x % split) : 0;
+  const int ks_begin = split > 1 ? crank * kstages_all / split : 0;
+  const int ks_end = split > 1 ? (crank + 1) * kstages_all / split : kstages_all;
+  const int kstages = ks_end - ks_begin;
+  const int kx0 = ks_begin * kPanelsPerStage * 64;                   // first column staged
+  const int kx = min(k, ks_end * kPanelsPerStage * 64) - kx0;        // columns staged
+  // Row stride of the staged activations: the largest member's share, so the
+  // shared-memory layout is the same in every member of a cluster (the
+  // members address member 0's barrier and sums by their own offsets).
+  const int kx_ld = split > 1
+                        ? min(k, (kstages_all + split - 1) / split * kPanelsPerStage * 64)
+                        : k;
+  const int g_first = split > 1 ? static_cast<int>(blockIdx.x / split) : static_cast<int>(blockIdx.x);
+  const int g_step = split > 1 ? n_groups : static_cast<int>(gridDim.x);
+
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  __half* xs = reinterpret_cast<__half*>(ring + stages * kStageBytes);  // [BT][k]
-  uint64_t* full = reinterpret_cast<uint64_t*>(xs + BT * k);
+  __half* xs = reinterpret_cast<__half*>(ring + stages * kStageBytes);  // [BT][kx_ld]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs + BT * kx_ld);
   uint64_t* empty = full + kMaxStages;
-  float* part_sum = reinterpret_cast<float*>(empty + kMaxStages);  // [4 warps][16 rows][2]
-  float* red = part_sum + 4 * kRows * 2;                        // [4 warps][BT]
-  int* red_id = reinterpret_cast<int*>(red + 4 * BT);          // [4 warps][BT]
-  float* rn = reinterpret_cast<float*>(red_id + 4 * BT);       // [BT] RMSNorm scale
-  int* pos_s = reinterpret_cast<int*>(rn + BT);                // [BT] positions
+  uint64_t* cl_bar = empty + kMaxStages;                           // member 0: others' sums landed
+  float* cl_part = reinterpret_cast<float*>(cl_bar + 1);           // [8 members][16 rows][2]
+  float* part_sum = cl_part + 8 * kRows * 2;                       // [4 warps][16 rows][2]
+  float* red = part_sum + 4 * kRows * 2;                           // [4 warps][BT]
+  int* red_id = reinterpret_cast<int*>(red + 4 * BT);             // [4 warps][BT]
+  float* rn = reinterpret_cast<float*>(red_id + 4 * BT);          // [BT] RMSNorm scale
+  int* pos_s = reinterpret_cast<int*>(rn + BT);                   // [BT] positions
   volatile int* abort_flag = pos_s + BT;
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int kstages = (kblocks + kPanelsPerStage - 1) / kPanelsPerStage;
 
   pdl_launch_dependents();
   if (t == 0) {
@@ -105,10 +125,12 @@ __global__ void __launch_bounds__(kGemvThreads)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers / 32);
     }
+    mbar_init(cl_bar, split > 1 ? split - 1 : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
+  if (split > 1) cluster_sync_all();  // member 0's barrier is initialised before anyone arrives
 
   if (warp == kConsumers / 32) {
     // Producer: the weights never depend on the previous kernel, so it streams
@@ -118,11 +140,11 @@ __global__ void __launch_bounds__(kGemvThreads)
     int it = 0, slot = 0;
     uint32_t phase = 0;  // phase of the current pass over the ring
     bool ok = true;
-    for (int g = blockIdx.x; g < n_groups && ok; g += gridDim.x) {
+    for (int g = g_first; g < n_groups && ok; g += g_step) {
       const int row0 = g * kRows;
       const uint8_t* base =
           w_packed + static_cast<size_t>(row0 >> 7) * kblocks * 16384 + (row0 & 127) * 128;
-      for (int ks = 0; ks < kstages; ++ks, ++it) {
+      for (int ks = ks_begin; ks < ks_end; ++ks, ++it) {
         if (!wait_or_abort(&empty[slot], phase ^ 1, abort_flag) || *abort_flag) {
           ok = false;
           break;
@@ -147,10 +169,10 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   // Consumers: activations, RMSNorm scale and positions of this step.
   pdl_wait();
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(x);
-    uint4* dst = reinterpret_cast<uint4*>(xs);
-    for (int i = t; i < BT * k / 8; i += kConsumers) dst[i] = src[i];
+  for (int b = 0; b < BT; ++b) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(b) * k + kx0);
+    uint4* dst = reinterpret_cast<uint4*>(xs + b * kx_ld);
+    for (int i = t; i < kx / 8; i += kConsumers) dst[i] = src[i];
   }
 #pragma unroll
   for (int b = 0; b < BT; ++b) {
@@ -178,7 +200,7 @@ __global__ void __launch_bounds__(kGemvThreads)
   const int b_tok = lane >> 2, b_k = 2 * (lane & 3);  // B fragment: token, k pair
   int slot = 0;
   uint32_t phase = 0;
-  for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
+  for (int g = g_first; g < n_groups; g += g_step) {
     // One accumulator per k-step of a panel: four independent MMA chains.
     float c[4][4];
 #pragma unroll
@@ -189,17 +211,17 @@ __global__ void __launch_bounds__(kGemvThreads)
         bad = true;
         *abort_flag = 1;
       }
-      const int kb = ks * kPanelsPerStage + warp;  // this warp's panel
+      const int kb = (ks_begin + ks) * kPanelsPerStage + warp;  // this warp's panel
       if (!bad && kb < kblocks) {
         const uint32_t slice = smem_u32(ring + slot * kStageBytes + warp * kSlice) + a_row * 128;
-        const __half* xk = xs + kb * 64 + b_k;
+        const __half* xk = xs + (kb * 64 - kx0) + b_k;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           uint32_t a0, a1, a2, a3, b0 = 0, b1 = 0;
           ldmatrix_x4(a0, a1, a2, a3, slice + (((2 * kk + a_chunk) ^ (a_row & 7)) << 4));
           if (b_tok < BT) {
-            b0 = *reinterpret_cast<const uint32_t*>(xk + b_tok * k + kk * 16);
-            b1 = *reinterpret_cast<const uint32_t*>(xk + b_tok * k + kk * 16 + 8);
+            b0 = *reinterpret_cast<const uint32_t*>(xk + b_tok * kx_ld + kk * 16);
+            b1 = *reinterpret_cast<const uint32_t*>(xk + b_tok * kx_ld + kk * 16 + 8);
           }
           mma_16816(c[kk], a0, a1, a2, a3, b0, b1);
         }
@@ -211,7 +233,13 @@ __global__ void __launch_bounds__(kGemvThreads)
         phase ^= 1;
       }
     }
-    if (consumer_sync_or(bad)) return;
+    if (consumer_sync_or(bad)) {
+      // Member 0 stays until every other member has arrived (they write into it).
+      if (split > 1 && crank == 0 && t == 0)
+        for (uint32_t i = 0; i < kMaxPolls && !mbar_try_wait_cluster(cl_bar, 0); ++i) {
+        }
+      return;
+    }
 
     // Add the four warps' sums (lanes 4i hold rows i and i + 8, tokens 0-1).
     if ((lane & 3) == 0) {
@@ -228,10 +256,34 @@ __global__ void __launch_bounds__(kGemvThreads)
     float acc[BT];
 #pragma unroll
     for (int b = 0; b < BT; ++b)
-      acc[b] = (((part_sum[row * 2 + b] + part_sum[(kRows + row) * 2 + b]) +
-                 part_sum[(2 * kRows + row) * 2 + b]) +
-                part_sum[(3 * kRows + row) * 2 + b]) *
-               rn[b];
+      acc[b] = ((part_sum[row * 2 + b] + part_sum[(kRows + row) * 2 + b]) +
+                part_sum[(2 * kRows + row) * 2 + b]) +
+               part_sum[(3 * kRows + row) * 2 + b];
+    if (split > 1) {
+      if (crank != 0) {
+        // Hand this member's sums to member 0 and leave.
+        if (lead) {
+          const uint32_t dst = cluster_map(smem_u32(cl_part + (crank * kRows + row) * 2), 0);
+#pragma unroll
+          for (int b = 0; b < BT; ++b) st_cluster_f32(dst + 4 * b, acc[b]);
+        }
+        consumer_sync();
+        if (t == 0) mbar_arrive_cluster(cluster_map(smem_u32(cl_bar), 0));
+        return;
+      }
+      // Member 0: the other members' sums, added in member order.
+      bool landed = false;
+      for (uint32_t i = 0; i < kMaxPolls && !landed; ++i) landed = mbar_try_wait_cluster(cl_bar, 0);
+      if (!landed) {
+        report_error(kDevErrTmaTimeout);
+        return;
+      }
+#pragma unroll
+      for (int b = 0; b < BT; ++b)
+        for (int m = 1; m < split; ++m) acc[b] += cl_part[(m * kRows + row) * 2 + b];
+    }
+#pragma unroll
+    for (int b = 0; b < BT; ++b) acc[b] *= rn[b];
     const int n = g * kRows + row;         // row of W
     const int tile = n >> 7, p = n & 127;  // 128-row tile and row within it
 
@@ -254,6 +306,39 @@ __global__ void __launch_bounds__(kGemvThreads)
         }
       }
     } else if (ep.kind == kEpiResid) {
+      // Tensor parallel: all-reduce first.  The lead thread stores this rank's
+      // partial as a tagged word, reads every rank's word for (b, n) over
+      // NVLink (all loads in flight at once, re-reading late ones) and adds
+      // them in rank order, as every rank does.
+      if (ep.px.seq >= 0 && lead) {
+        const uint32_t tag = px_tag(ep.px, ep.px.seq);
+#pragma unroll
+        for (int b = 0; b < BT; ++b)
+          if (b < ep.batch) px_store(ep.px, tag, b, n, acc[b]);
+        uint64_t wv[BT][kMaxRanks];
+#pragma unroll
+        for (int b = 0; b < BT; ++b)
+#pragma unroll
+          for (int r = 0; r < kMaxRanks; ++r)
+            wv[b][r] = (b < ep.batch && r < ep.px.ranks)
+                           ? ld_relaxed_sys(ep.px.part[r] + px_offset(ep.px, b, n))
+                           : 0;
+#pragma unroll
+        for (int b = 0; b < BT; ++b) {
+          float sum = 0.f;
+#pragma unroll
+          for (int r = 0; r < kMaxRanks; ++r) {
+            if (b < ep.batch && r < ep.px.ranks) {
+              uint32_t bits = static_cast<uint32_t>(wv[b][r]);
+              if (static_cast<uint32_t>(wv[b][r] >> 32) != tag &&
+                  !px_get(ep.px.part[r] + px_offset(ep.px, b, n), tag, &bits))
+                bits = 0;
+              sum += __uint_as_float(bits);
+            }
+          }
+          acc[b] = sum;
+        }
+      }
       // Residual add, next norm's input, and the group's sum of squares.
       const float w = __half2float(ep.norm_w[n]);
 #pragma unroll
@@ -362,31 +447,54 @@ __global__ void __launch_bounds__(kGemvThreads)
 }
 
 template <int BT>
-size_t gemv_smem(int k, int stages) {
-  // ring + staged activations + full/empty barriers + reduction scratch
-  return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(BT) * k * 2 +
-         2 * kMaxStages * 8 + (4 * kRows * 2 + 4 * BT + 4 * BT + BT + BT + 1) * 4 + 64;
+size_t gemv_smem(int kx, int stages) {
+  // ring + staged activations + full/empty/cluster barriers + member sums +
+  // reduction scratch
+  return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(BT) * kx * 2 +
+         (2 * kMaxStages + 1) * 8 +
+         (8 * kRows * 2 + 4 * kRows * 2 + 4 * BT + 4 * BT + BT + BT + 1) * 4 + 64;
 }
 
 struct GemvLaunch {
-  int grid = 0, stages = 0;
+  int grid = 0, stages = 0, split = 1;
 };
 
-// One wave of persistent CTAs.  For 1-4 CTAs per SM take the deepest ring
-// that fits and spread the groups so every CTA walks the same number (+-1);
-// keep the choice with the most bytes in flight up to 12 MB (about where bulk
-// streams saturate HBM), then the most CTAs, then the deepest ring.
+// Enough groups to fill every SM twice: one wave of persistent CTAs.  For 1-4
+// CTAs per SM take the deepest ring that fits and spread the groups so every
+// CTA walks the same number (+-1); keep the choice with the most bytes in
+// flight up to 12 MB (about where bulk streams saturate HBM), then the most
+// CTAs, then the deepest ring.  Fewer groups: split K over clusters of 2-8
+// CTAs until there are two CTAs per SM or the K shares get short.
 template <int BT>
 GemvLaunch choose_launch(int n_rows, int k) {
   const int n_groups = n_rows / kRows;
-  const size_t fixed = gemv_smem<BT>(k, 0);
+  const int kstages = (k / 64 + kPanelsPerStage - 1) / kPanelsPerStage;
+  const int sms = sm_count();
   GemvLaunch best;
+  int split = 1;
+  // Double while that leaves at least 2 stages per member (splitting short K
+  // only adds the reduction).
+  while (split < 8 && n_groups * split < 2 * sms && kstages >= 4 * split) split *= 2;
+  if (split > 1) {
+    const int grid = n_groups * split;
+    const int kx = std::min(k, (kstages + split - 1) / split * kPanelsPerStage * 64);
+    const int per_sm = std::min(4, (grid + sms - 1) / sms);
+    const long long avail = kGemvSmemPerSm / per_sm - kGemvSmemReserved -
+                            static_cast<long long>(gemv_smem<BT>(kx, 0));
+    const int slice = (kstages + split - 1) / split;
+    best.grid = grid;
+    best.split = split;
+    best.stages = static_cast<int>(std::min<long long>({kMaxStages, slice, avail / kStageBytes}));
+    if (best.stages >= 1) return best;
+    best = GemvLaunch();
+  }
+  const size_t fixed = gemv_smem<BT>(k, 0);
   long long best_score = -1;
   for (int per_sm = 1; per_sm <= 4; ++per_sm) {
     const long long avail = kGemvSmemPerSm / per_sm - kGemvSmemReserved - static_cast<long long>(fixed);
     const int stages = static_cast<int>(std::min<long long>(kMaxStages, avail / kStageBytes));
     if (stages < 4) break;
-    const int slots = per_sm * sm_count();
+    const int slots = per_sm * sms;
     const int rounds = (n_groups + slots - 1) / slots;
     const int grid = (n_groups + rounds - 1) / rounds;
     const long long score =
@@ -406,18 +514,23 @@ int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams
                 cudaStream_t stream, bool pdl) {
   const GemvLaunch g = choose_launch<BT>(n_rows, k);
   NPU_REQUIRE(g.grid > 0, "gemv: activations of K=%d leave no room for the ring", k);
-  const size_t smem = gemv_smem<BT>(k, g.stages);
+  const int kstages = (k / 64 + kPanelsPerStage - 1) / kPanelsPerStage;
+  const int kx = g.split > 1 ? std::min(k, (kstages + g.split - 1) / g.split * kPanelsPerStage * 64) : k;
+  const size_t smem = gemv_smem<BT>(kx, g.stages);
   auto kern = gemv_kernel<BT>;
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
+  if (g.split > 1)
+    NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   LaunchCfg cfg;
   cfg.grid = dim3(g.grid);
   cfg.block = dim3(kGemvThreads);
   cfg.smem = smem;
   cfg.stream = stream;
   cfg.pdl = pdl;
+  cfg.cluster = g.split;
   return launch(cfg, kern, static_cast<const uint8_t*>(w), static_cast<const __half*>(x), ep, k,
-                k / 64, n_rows / kRows, g.stages);
+                k / 64, n_rows / kRows, g.stages, g.split);
 }
 
 }  // namespace

@@ -891,10 +891,12 @@ int proj_run(const void* w, bool w_packed, const void* x, int n_rows, int k, int
   if (ep.kind == kEpiStore)
     NPU_REQUIRE(ep.out != nullptr || ep.px.seq >= 0, "projection: null output");
   if (ep.px.seq >= 0)
-    NPU_REQUIRE(ep.kind == kEpiStore && ep.px.ranks >= 1 && ep.px.ranks <= kMaxRanks &&
-                    ep.px.seq < kArgmaxSeq && ep.n_rows == ep.px.hidden &&
-                    batch <= ep.px.max_batch && ep.px.epoch,
-                "projection: peer exchange needs a STORE of all hidden rows");
+    NPU_REQUIRE((ep.kind == kEpiStore || (ep.kind == kEpiResid && w_packed &&
+                                          gemv_supported(n_rows, k, batch, ep))) &&
+                    ep.px.ranks >= 1 && ep.px.ranks <= kMaxRanks && ep.px.seq < kArgmaxSeq &&
+                    ep.n_rows == ep.px.hidden && batch <= ep.px.max_batch && ep.px.epoch,
+                "projection: peer exchange needs a STORE of all hidden rows, or a residual "
+                "epilogue on the GEMV path");
   NPU_REQUIRE(ep.kind >= kEpiStore && ep.kind <= kEpiArgmax, "projection: unknown epilogue %d",
               ep.kind);
   NPU_REQUIRE(ep.ssq_in == nullptr || (ep.ssq_parts >= 1 && ep.ssq_ld >= batch),

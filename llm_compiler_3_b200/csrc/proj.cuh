@@ -69,8 +69,9 @@ struct EpiParams {
   int am_ld = 0;
   int am_rows = 128;          // rows per partial (max, argmax): 128 or 16
 
-  // kEpiStore with px.seq >= 0: instead of `out`, store the FP32 value in this
-  // rank's exchange buffer and raise the row-group flags on every rank (peer.cuh).
+  // px.seq >= 0, kEpiStore: instead of `out`, store the FP32 value as a tagged
+  // word in this rank's exchange buffer (peer.cuh); kEpiResid (GEMV path only):
+  // all-reduce the partial over the ranks before the residual add.
   PeerExchange px;
 };
 

@@ -700,18 +700,27 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
   EpiParams e;
   e.n_rows = P.hidden;
   e.batch = batch;
-  if (c->tp_size == 1) {
-    e.kind = kEpiResid;
-    e.resid = c->resid;
-    e.ld_resid = P.hidden;
-    e.norm_w = next_norm;
-    e.xw = c->xw;
-    e.ld_xw = P.hidden;
-    e.ssq_out = c->ssq;
-    e.ssq_out_ld = P.max_batch;
-    e.ssq_out_rows = part_rows(batch);
+  e.kind = kEpiResid;
+  e.resid = c->resid;
+  e.ld_resid = P.hidden;
+  e.norm_w = next_norm;
+  e.xw = c->xw;
+  e.ld_xw = P.hidden;
+  e.ssq_out = c->ssq;
+  e.ssq_out_ld = P.max_batch;
+  e.ssq_out_rows = part_rows(batch);
+  if (c->tp_size == 1)
+    return proj_run(w, true, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
+  // Batch 1-2 with peer exchange: the GEMV's residual epilogue all-reduces
+  // the partials itself (no separate kernel).
+  if (c->px_ready && gemv_supported(P.hidden, k, batch, e)) {
+    e.px = c->px;
+    e.px.seq = seq;
     return proj_run(w, true, x, P.hidden, k, batch, e, c->proj_ws, c->proj_ws_bytes, s, true);
   }
+  e = EpiParams();
+  e.n_rows = P.hidden;
+  e.batch = batch;
   e.kind = kEpiStore;
   e.out = c->partial;
   e.ld_out = P.hidden;

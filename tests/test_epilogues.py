@@ -48,12 +48,14 @@ def _interleave(gate, up):
 
 @pytest.mark.parametrize("batch", [1, 2, 16, 64])
 @pytest.mark.parametrize("packed", [False, True])
-def test_packed_weights(cuda, batch, packed):
+@pytest.mark.parametrize("rows", [6144 + 64, 768])
+def test_packed_weights(cuda, batch, packed, rows):
     """Panels give the bit-identical tensor-core result; at batch 1-2 packed
-    weights run the CUDA-core GEMV, checked against the oracle."""
+    weights run the GEMV (768 rows: K split over clusters of 8), checked
+    against the oracle."""
     from llm_compiler_3_b200 import _native, ops
     x = seeded((batch, 4096), 1)
-    w = seeded((6144 + 64, 4096), 2, 0.02)     # partial last tile
+    w = seeded((rows, 4096), 2, 0.02)          # 6208: partial last tile
     ref = ops.linear(x.cuda(), w.cuda(), out_dtype=torch.float32)
     e = _native.Epilogue(kind=_native.EPI_STORE, ld_out=w.shape[0], out_f32=1)
     out = torch.empty(batch, w.shape[0], dtype=torch.float32, device="cuda")
@@ -133,9 +135,12 @@ def test_qkv_rope_append(cuda, batch, qk_norm, packed):
 @pytest.mark.parametrize("batch", [1, 2, 16, 64])
 @pytest.mark.parametrize("rows", [128, 16])
 @pytest.mark.parametrize("packed", [False, True])
-def test_residual_and_next_norm(cuda, batch, rows, packed):
+@pytest.mark.parametrize("K", [512, 384, 1280])
+def test_residual_and_next_norm(cuda, batch, rows, packed, K):
+    """K 384 / 1280 split unevenly over the GEMV's cluster members (a partial
+    last stage; 1-2 stages per member)."""
     from llm_compiler_3_b200 import _native, ops
-    H, K = 1024, 512
+    H = 1024
     x = seeded((batch, K), 11)
     w = seeded((H, K), 12, 0.05)
     resid = seeded((batch, H), 13).float()
