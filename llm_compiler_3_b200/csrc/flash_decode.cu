@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                         const int32_t* __restrict__ seq_lens, __half* __restrict__ out,
                         float* __restrict__ part, uint32_t* __restrict__ counters, int q_heads,
                         int kv_heads, int max_seq, int keys_per_split, int num_splits,
-                        float scale_log2) {
+                        float scale_log2, const int32_t* __restrict__ positions) {
   using S = FdShape<D>;
   constexpr int KSTEPS = D / 16;  // k-steps of the score MMA
   constexpr int DBLK = D / 16;    // 16-dim blocks of the PV MMA
@@ -84,10 +84,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // The next kernel may be scheduled once every CTA of this grid is resident;
   // it waits for this grid's results itself.
   pdl_launch_dependents();
-  // Everything below reads what the previous kernel (the KV append) wrote.
-  pdl_wait();
-
-  int len = seq_lens[b];
+  // With `positions` (the step's own input, written before the step) the
+  // attended length is positions[b] + 1 and is known before the previous
+  // kernel (the KV append) finishes: key tiles that end before the new key
+  // were written by earlier steps and are loaded before waiting for it.
+  // Without, the length comes from seq_lens, which may be the previous
+  // kernel's output.
+  if (positions == nullptr) pdl_wait();
+  int len = positions != nullptr ? positions[b] + 1 : seq_lens[b];
   len = len < 0 ? 0 : (len > max_seq ? max_seq : len);
   const int k_begin = split * keys_per_split;
   const int k_end = min(len, k_begin + keys_per_split);
@@ -110,8 +114,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   };
 
+  int issued = 0;
+  if (positions != nullptr) {
+    if (lane == 0)
+      for (; issued < my_tiles && issued < STAGES; ++issued)
+        if (k_begin + (warp + issued * WARPS + 1) * kKeysPerTile > len - 1) break;  // holds the new key
+        else issue(issued);
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    pdl_wait();  // q and the new key come from the previous kernel
+  }
   if (lane == 0) {
-    for (int i = 0; i < my_tiles && i < STAGES; ++i) issue(i);
+    for (int i = issued; i < my_tiles && i < STAGES; ++i) issue(i);
   }
 
   // Q^T fragments (B operand of the score MMA): column n = query head g of the
@@ -456,7 +469,8 @@ size_t workspace_bytes_for(int batch, int kv_heads, int head_dim, int splits) {
 template <int D>
 int launch_fd(const CUtensorMap& km, const CUtensorMap& vm, const __half* q, const int32_t* lens,
               __half* out, float* part, uint32_t* counters, int batch, int q_heads, int kv_heads,
-              int max_seq, int kps, int splits, float scale_log2, cudaStream_t stream, bool pdl) {
+              int max_seq, int kps, int splits, float scale_log2, cudaStream_t stream, bool pdl,
+              const int32_t* positions) {
   auto kern = flash_decode_kernel<D, kWarps, kStages>;
   constexpr size_t smem = fd_smem_bytes<D>();
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -468,17 +482,20 @@ int launch_fd(const CUtensorMap& km, const CUtensorMap& vm, const __half* q, con
   cfg.stream = stream;
   cfg.pdl = pdl;
   return launch(cfg, kern, km, vm, q, lens, out, part, counters, q_heads, kv_heads, max_seq, kps,
-                splits, scale_log2);
+                splits, scale_log2, positions);
 }
 
 }  // namespace
 
-// Internal entry used by the decode runtime as well as the C ABI.
+// Internal entry used by the decode runtime as well as the C ABI.  With
+// `positions` (the decode step's input, seq_lens[b] == positions[b] + 1) the
+// kernel starts loading the keys cached by earlier steps before the previous
+// kernel finishes.
 int flash_decode_run(const void* q, const void* k, const void* v, const int32_t* seq_lens,
                      void* out, int batch, int q_heads, int kv_heads, int head_dim, int max_seq,
                      float scale, int num_splits, void* workspace, size_t workspace_bytes,
-                     cudaStream_t stream, bool pdl) {
-  NPU_REQUIRE(q && k && v && seq_lens && out, "flash_decode: null tensor pointer");
+                     cudaStream_t stream, bool pdl, const int32_t* positions) {
+  NPU_REQUIRE(q && k && v && (seq_lens || positions) && out, "flash_decode: null tensor pointer");
   NPU_REQUIRE(batch >= 1 && batch <= 65535, "flash_decode: batch %d out of range", batch);
   NPU_REQUIRE(kv_heads >= 1 && kv_heads <= 65535 && q_heads >= kv_heads && q_heads % kv_heads == 0,
               "flash_decode: q_heads %d is not a multiple of kv_heads %d", q_heads, kv_heads);
@@ -521,9 +538,9 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
   __half* oh = static_cast<__half*>(out);
   if (head_dim == 128)
     return launch_fd<128>(km, vm, qh, seq_lens, oh, part, counters, batch, q_heads, kv_heads,
-                          max_seq, kps, splits, scale_log2, stream, pdl);
+                          max_seq, kps, splits, scale_log2, stream, pdl, positions);
   return launch_fd<64>(km, vm, qh, seq_lens, oh, part, counters, batch, q_heads, kv_heads,
-                       max_seq, kps, splits, scale_log2, stream, pdl);
+                       max_seq, kps, splits, scale_log2, stream, pdl, positions);
 }
 
 size_t flash_decode_workspace(int batch, int kv_heads, int head_dim, int max_seq, int num_splits) {
@@ -547,7 +564,8 @@ extern "C" int npu_b200_flash_decode(const void* d_q, const void* d_k, const voi
   npu_b200::clear_error();
   return npu_b200::flash_decode_run(d_q, d_k, d_v, d_seq_lens, d_out, batch, q_heads, kv_heads,
                                     head_dim, max_seq, scale, num_splits, d_workspace,
-                                    workspace_bytes, static_cast<cudaStream_t>(stream), false);
+                                    workspace_bytes, static_cast<cudaStream_t>(stream), false,
+                                    nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -610,5 +628,6 @@ extern "C" int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, c
     NPU_TRY_CUDA(cudaMemsetAsync(scratch, 0, units * sizeof(uint32_t), s));
   }
   return flash_decode_run(d_q, d_k, d_v, d_seq_lens, d_out, batch, q_heads, kv_heads, head_dim,
-                          max_seq, scale, num_splits, scratch, kNoAllocScratchBytes, s, false);
+                          max_seq, scale, num_splits, scratch, kNoAllocScratchBytes, s, false,
+                          nullptr);
 }

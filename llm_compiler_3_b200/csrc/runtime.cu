@@ -47,7 +47,7 @@ namespace npu_b200 {
 int flash_decode_run(const void* q, const void* k, const void* v, const int32_t* seq_lens,
                      void* out, int batch, int q_heads, int kv_heads, int head_dim, int max_seq,
                      float scale, int num_splits, void* workspace, size_t workspace_bytes,
-                     cudaStream_t stream, bool pdl);
+                     cudaStream_t stream, bool pdl, const int32_t* positions);
 size_t flash_decode_workspace(int batch, int kv_heads, int head_dim, int max_seq, int num_splits);
 
 namespace {
@@ -807,7 +807,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
       return rc;
     if ((rc = flash_decode_run(c->q_buf, L.k_cache, L.v_cache, c->d_seq_lens, c->attn, batch,
                                c->q_loc, c->kv_loc, D, P.max_seq, 1.f / sqrtf(static_cast<float>(D)),
-                               0, c->fd_ws, c->fd_ws_bytes, s, true)))
+                               0, c->fd_ws, c->fd_ws_bytes, s, true, c->d_positions)))
       return rc;
     if ((rc = residual_out(c, L.w_o, c->attn, c->q_loc * D, batch, L.post_norm, 2 * l, s)))
       return rc;
