@@ -145,67 +145,73 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def cpu_baseline(batch, layers, seq, samples=3):
+class CpuOracleStep:
     """The oracle (PyTorch on the host CPU, FP16 storage, FP32 compute) on a bounded
-    sample: one decoder layer and the LM head at the full batch and cache length,
-    extrapolated to the whole stack."""
-    import torch
-    import oracle
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    shape = oracle.LLAMA3_8B
-    g = torch.Generator().manual_seed(5)
+    sample of the decode step: one decoder layer and the LM head at the full batch
+    and cache length, extrapolated to the whole stack.  Inputs are built once."""
 
-    def h(*s, std=0.02):
-        return (torch.randn(*s, generator=g) * std).half()
+    def __init__(self, batch, layers, seq):
+        import torch
+        import oracle
+        self.torch, self.oracle = torch, oracle
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.batch, self.layers, self.seq = batch, layers, seq
+        self.shape = oracle.LLAMA3_8B
+        g = torch.Generator().manual_seed(5)
 
-    w = {"self_attn.q_proj.weight": h(HEADS * HEAD_DIM, HIDDEN),
-         "self_attn.k_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
-         "self_attn.v_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
-         "self_attn.o_proj.weight": h(HIDDEN, HEADS * HEAD_DIM),
-         "mlp.gate_proj.weight": h(FFN, HIDDEN), "mlp.up_proj.weight": h(FFN, HIDDEN),
-         "mlp.down_proj.weight": h(HIDDEN, FFN),
-         "input_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16),
-         "post_attention_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16)}
-    k = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
-    v = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
-    lm = h(VOCAB, HIDDEN)
-    x = h(batch, HIDDEN, std=1.0)
-    pos = torch.full((batch,), seq - 1, dtype=torch.int32)
-    times = []
-    for _ in range(samples):
+        def h(*s, std=0.02):
+            return (torch.randn(*s, generator=g) * std).half()
+
+        self.w = {"self_attn.q_proj.weight": h(HEADS * HEAD_DIM, HIDDEN),
+                  "self_attn.k_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
+                  "self_attn.v_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
+                  "self_attn.o_proj.weight": h(HIDDEN, HEADS * HEAD_DIM),
+                  "mlp.gate_proj.weight": h(FFN, HIDDEN), "mlp.up_proj.weight": h(FFN, HIDDEN),
+                  "mlp.down_proj.weight": h(HIDDEN, FFN),
+                  "input_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16),
+                  "post_attention_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16)}
+        self.k = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
+        self.v = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
+        self.lm = h(VOCAB, HIDDEN)
+        self.x = h(batch, HIDDEN, std=1.0)
+        self.pos = torch.full((batch,), seq - 1, dtype=torch.int32)
+        self.sample = (f"oracle: 1 of {layers} layers + LM head at batch {batch}, {seq} keys, "
+                       f"x{layers} layers")
+
+    def seconds_per_step(self):
+        o, torch = self.oracle, self.torch
         t0 = time.perf_counter()
-        y, _, _ = oracle.decoder_layer_decode(w, x, pos, k, v, shape, write_cache=False)
+        y, _, _ = o.decoder_layer_decode(self.w, self.x, self.pos, self.k, self.v, self.shape,
+                                         write_cache=False)
         t1 = time.perf_counter()
-        logits = oracle.linear(oracle.rms_norm(y, torch.ones(HIDDEN), shape.eps), lm)
-        oracle.greedy_argmax(logits)
+        logits = o.linear(o.rms_norm(y, torch.ones(HIDDEN), self.shape.eps), self.lm)
+        o.greedy_argmax(logits)
         t2 = time.perf_counter()
-        times.append((t1 - t0) * layers + (t2 - t1))
-    t_step = statistics.median(times)
-    return {"value": batch / t_step, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"oracle: 1 of {layers} layers + LM head at batch {batch}, {seq} keys, "
-                      f"x{layers} layers, median of {samples}",
-            "seconds_per_step": t_step}
+        return (t1 - t0) * self.layers + (t2 - t1)
+
+
+def cpu_baseline(batch, layers, seq, samples=3):
+    step = CpuOracleStep(batch, layers, seq)
+    t_step = statistics.median(step.seconds_per_step() for _ in range(samples))
+    return {"value": batch / t_step, "unit": "tokens/s", "cores": step.threads, "kind": "port",
+            "sample": f"{step.sample}, median of {samples}", "seconds_per_step": t_step}
 
 
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    steps = []
-    base = None
-    for i in range(a.warmup + a.steps):
-        base = cpu_baseline(a.batch, a.layers, a.seq, samples=1)
-        if i >= a.warmup:
-            steps.append(base["seconds_per_step"])
-    t = statistics.median(steps)
+    step = CpuOracleStep(a.batch, a.layers, a.seq)
+    times = [step.seconds_per_step() for _ in range(a.warmup + a.steps)][a.warmup:]
+    t = statistics.median(times)
     value = a.batch / t
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s",
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": t * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic", "config": workload_config(a),
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"],
-                             "kind": "port", "sample": base["sample"]},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": step.threads,
+                             "kind": "port", "sample": f"{step.sample}, median of {a.steps}"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -397,7 +403,9 @@ def run_b200(a):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": t_step * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (random-init weights N(0,0.02), KV cache N(0,1), seeded on device)",
-        "config": workload_config(a),
+        "config": dict(workload_config(a), **({"tp_exchange": "nvlink peer memory"
+                                                 if info.get("peer_exchange") else "nccl"}
+                                                if world > 1 else {})),
         "roofline": {"bound": "hbm", "kernel": "flash_decode", "achieved": fd_achieved,
                      "peak": peak, "unit": "GB/s", "frac": fd_achieved / peak,
                      "peak_source": peak_kind, "traffic": traffic,
