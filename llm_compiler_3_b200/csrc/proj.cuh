@@ -90,6 +90,7 @@ bool gemv_supported(int n_rows, int k, int batch, const EpiParams& ep);
 int gemv_run(const void* w_packed, const void* x, int n_rows, int k, int batch, const EpiParams& ep,
              cudaStream_t stream, bool pdl);
 
+
 // Weight panels: 16 KB blocks [ceil(n/128)][k/64] of 128 rows x 64 columns,
 // each already in the 128-byte-swizzled K-major layout the tensor cores read,
 // so one contiguous bulk copy moves a block from HBM to shared memory.

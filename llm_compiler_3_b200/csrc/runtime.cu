@@ -755,6 +755,91 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
   return residual_update(u, s, c->px_ready);  // PDL only after our own kernel, not NCCL
 }
 
+EpiParams qkv_epi(const npu_b200_ctx* c, int l, int batch) {
+  const Plan& P = c->plan;
+  const LayerBuffers& L = c->layers[l];
+  const int D = P.head_dim;
+  EpiParams q;
+  q.kind = kEpiQKV;
+  q.n_rows = (c->q_loc + 2 * c->kv_loc) * D;
+  q.batch = batch;
+  norm_input(c, batch, &q);
+  q.out = c->q_buf;
+  q.ld_out = c->q_loc * D;
+  q.q_heads = c->q_loc;
+  q.kv_heads = c->kv_loc;
+  q.positions = c->d_positions;
+  q.inv_freq = c->d_inv_freq;
+  q.rope_tab = c->rope_tab;
+  q.k_cache = L.k_cache;
+  q.v_cache = L.v_cache;
+  q.max_seq = P.max_seq;
+  q.cache_batch_stride = c->kv_loc * P.max_seq * D;
+  q.q_norm_w = L.q_norm;
+  q.k_norm_w = L.k_norm;
+  q.qk_eps = P.eps;
+  return q;
+}
+
+EpiParams swiglu_epi(const npu_b200_ctx* c, int batch) {
+  EpiParams g;
+  g.kind = kEpiSwiGLU;
+  g.n_rows = 2 * c->ffn_loc;
+  g.batch = batch;
+  norm_input(c, batch, &g);
+  g.out = c->act;
+  g.ld_out = c->ffn_loc;
+  return g;
+}
+
+EpiParams argmax_epi(const npu_b200_ctx* c, int batch) {
+  EpiParams a;
+  a.kind = kEpiArgmax;
+  a.n_rows = c->vocab_loc;
+  a.batch = batch;
+  norm_input(c, batch, &a);
+  a.am_val = c->am_val;
+  a.am_idx = c->am_idx;
+  a.am_ld = c->plan.max_batch;
+  a.am_rows = part_rows(batch);
+  return a;
+}
+
+const __half* norm_after(const npu_b200_ctx* c, int l) {
+  const Plan& P = c->plan;
+  return l + 1 < P.layers ? c->layers[l + 1].in_norm
+                          : (c->final_norm ? c->final_norm : c->layers[l].in_norm);
+}
+
+// The greedy-id tail of a token step: reduce the LM head's partial argmaxes
+// (and across ranks).
+int finish_argmax(npu_b200_ctx* c, int batch, cudaStream_t s) {
+  const Plan& P = c->plan;
+  const int rows = part_rows(batch);
+  const int lm_tiles = (c->vocab_loc + rows - 1) / rows;
+  int rc = 0;
+  if (c->tp_size == 1)
+    return argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
+                         c->gather_send, c->d_ids, s, true);
+  if (c->px_ready) {
+    PeerExchange x = c->px;
+    x.seq = kArgmaxSeq;
+    if ((rc = argmax_reduce_push(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch,
+                                 c->vocab_off, x, s, true)))
+      return rc;
+    return argmax_combine_peers(x, batch, c->d_ids, s, true);
+  }
+  if ((rc = argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
+                          c->gather_send, reinterpret_cast<int32_t*>(c->gather_send + P.max_batch),
+                          s, true)))
+    return rc;
+  if ((rc = check_nccl(g_nccl.AllGather(c->gather_send, c->gather_recv, 2 * P.max_batch,
+                                        ncclFloat32, c->comm, s),
+                       "ncclAllGather")))
+    return rc;
+  return argmax_combine(c->gather_recv, c->tp_size, P.max_batch, batch, c->d_ids, s, false);
+}
+
 int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
   const Plan& P = c->plan;
   const int H = P.hidden, D = P.head_dim;
@@ -783,25 +868,7 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
   }
   for (int l = 0; l < P.layers; ++l) {
     LayerBuffers& L = c->layers[l];
-    EpiParams q;
-    q.kind = kEpiQKV;
-    q.n_rows = (c->q_loc + 2 * c->kv_loc) * D;
-    q.batch = batch;
-    norm_input(c, batch, &q);
-    q.out = c->q_buf;
-    q.ld_out = c->q_loc * D;
-    q.q_heads = c->q_loc;
-    q.kv_heads = c->kv_loc;
-    q.positions = c->d_positions;
-    q.inv_freq = c->d_inv_freq;
-    q.rope_tab = c->rope_tab;
-    q.k_cache = L.k_cache;
-    q.v_cache = L.v_cache;
-    q.max_seq = P.max_seq;
-    q.cache_batch_stride = c->kv_loc * P.max_seq * D;
-    q.q_norm_w = L.q_norm;
-    q.k_norm_w = L.k_norm;
-    q.qk_eps = P.eps;
+    const EpiParams q = qkv_epi(c, l, batch);
     if ((rc = proj_run(L.w_qkv, true, c->xw, q.n_rows, H, batch, q, c->proj_ws, c->proj_ws_bytes, s,
                        true)))
       return rc;
@@ -811,57 +878,20 @@ int enqueue_step(npu_b200_ctx* c, int mode, int batch, cudaStream_t s) {
       return rc;
     if ((rc = residual_out(c, L.w_o, c->attn, c->q_loc * D, batch, L.post_norm, 2 * l, s)))
       return rc;
-    EpiParams g;
-    g.kind = kEpiSwiGLU;
-    g.n_rows = 2 * c->ffn_loc;
-    g.batch = batch;
-    norm_input(c, batch, &g);
-    g.out = c->act;
-    g.ld_out = c->ffn_loc;
+    const EpiParams g = swiglu_epi(c, batch);
     if ((rc = proj_run(L.w_gu, true, c->xw, g.n_rows, H, batch, g, c->proj_ws, c->proj_ws_bytes, s,
                        true)))
       return rc;
-    const __half* next = l + 1 < P.layers ? c->layers[l + 1].in_norm
-                                          : (c->final_norm ? c->final_norm : L.in_norm);
-    if ((rc = residual_out(c, L.w_down, c->act, c->ffn_loc, batch, next, 2 * l + 1, s)))
+    if ((rc = residual_out(c, L.w_down, c->act, c->ffn_loc, batch, norm_after(c, l), 2 * l + 1, s)))
       return rc;
   }
   if (mode == kModeHidden)
     return store_hidden(c->resid, c->hidden_io, static_cast<size_t>(batch) * H, s, true);
-
-  EpiParams a;
-  a.kind = kEpiArgmax;
-  a.n_rows = c->vocab_loc;
-  a.batch = batch;
-  norm_input(c, batch, &a);
-  a.am_val = c->am_val;
-  a.am_idx = c->am_idx;
-  a.am_ld = P.max_batch;
-  a.am_rows = part_rows(batch);
+  const EpiParams a = argmax_epi(c, batch);
   if ((rc = proj_run(c->lm_head, true, c->xw, c->vocab_loc, H, batch, a, c->proj_ws, c->proj_ws_bytes,
                      s, true)))
     return rc;
-  const int lm_tiles = (c->vocab_loc + a.am_rows - 1) / a.am_rows;
-  if (c->tp_size == 1)
-    return argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
-                         c->gather_send, c->d_ids, s, true);
-  if (c->px_ready) {
-    PeerExchange x = c->px;
-    x.seq = kArgmaxSeq;
-    if ((rc = argmax_reduce_push(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch,
-                                 c->vocab_off, x, s, true)))
-      return rc;
-    return argmax_combine_peers(x, batch, c->d_ids, s, true);
-  }
-  if ((rc = argmax_reduce(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch, c->vocab_off,
-                          c->gather_send, reinterpret_cast<int32_t*>(c->gather_send + P.max_batch),
-                          s, true)))
-    return rc;
-  if ((rc = check_nccl(g_nccl.AllGather(c->gather_send, c->gather_recv, 2 * P.max_batch,
-                                        ncclFloat32, c->comm, s),
-                       "ncclAllGather")))
-    return rc;
-  return argmax_combine(c->gather_recv, c->tp_size, P.max_batch, batch, c->d_ids, s, false);
+  return finish_argmax(c, batch, s);
 }
 
 int graph_for(npu_b200_ctx* c, int mode, int batch, cudaGraphExec_t* out) {
