@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                         const int32_t* __restrict__ seq_lens, __half* __restrict__ out,
                         float* __restrict__ part, uint32_t* __restrict__ counters, int q_heads,
                         int kv_heads, int max_seq, int keys_per_split, int num_splits,
-                        float scale_log2, const int32_t* __restrict__ positions) {
+                        float scale_log2, const int32_t* __restrict__ positions, int clustered) {
   using S = FdShape<D>;
   constexpr int KSTEPS = D / 16;  // k-steps of the score MMA
   constexpr int DBLK = D / 16;    // 16-dim blocks of the PV MMA
@@ -307,7 +307,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __syncthreads();
 
   const size_t unit = static_cast<size_t>(b) * kv_heads + h;
-  float* my_part = part + (unit * num_splits + split) * S::kPartFloats;
+  // Clustered (small batch): the splits of one (sequence, KV head) are one
+  // thread-block cluster; each keeps its partial in its own shared memory and
+  // member 0 merges them through distributed shared memory.
+  float* cp_o = co + WARPS * kMaxGroup * D;  // [8][D] this CTA's O
+  float* cp_m = cp_o + kMaxGroup * D;        // [8] max (log2 domain)
+  float* cp_l = cp_m + kMaxGroup;            // [8] row sums
+  float* my_part = clustered ? nullptr : part + (unit * num_splits + split) * S::kPartFloats;
   for (int idx = threadIdx.x; idx < group * D; idx += WARPS * 32) {
     const int head = idx / D, dim = idx - head * D;
     float mx = -INFINITY;
@@ -324,6 +330,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (num_splits == 1) {
       out[(static_cast<size_t>(b) * q_heads + h * group + head) * D + dim] =
           __float2half_rn(L > 0.f ? O / L : 0.f);
+    } else if (clustered) {
+      cp_o[head * D + dim] = O;
+      if (dim == 0) {
+        cp_m[head] = mx;
+        cp_l[head] = L;
+      }
     } else {
       my_part[head * D + dim] = O;
       if (dim == 0) {
@@ -333,6 +345,41 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
   }
   if (num_splits == 1) return;
+
+  if (clustered) {
+    cluster_sync_all();  // every member's partial is in its shared memory
+    if (split == 0) {
+      for (int idx = threadIdx.x; idx < group * D; idx += WARPS * 32) {
+        const int head = idx / D, dim = idx - head * D;
+        float mr[8], lr[8], orr[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (r < num_splits) {
+            mr[r] = ld_cluster_f32(cluster_map(smem_u32(cp_m + head), r));
+            lr[r] = ld_cluster_f32(cluster_map(smem_u32(cp_l + head), r));
+            orr[r] = ld_cluster_f32(cluster_map(smem_u32(cp_o + head * D + dim), r));
+          } else {
+            mr[r] = -INFINITY;
+            lr[r] = orr[r] = 0.f;
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) mx = fmaxf(mx, mr[r]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float wt = mr[r] == -INFINITY ? 0.f : fast_exp2(mr[r] - mx);
+          L += lr[r] * wt;
+          O += orr[r] * wt;
+        }
+        out[(static_cast<size_t>(b) * q_heads + h * group + head) * D + dim] =
+            __float2half_rn(L > 0.f ? O / L : 0.f);
+      }
+    }
+    cluster_sync_all();  // no member leaves while member 0 reads its shared memory
+    return;
+  }
 
   // Last CTA of this (sequence, KV head) merges every split.
   __threadfence();
@@ -470,7 +517,7 @@ template <int D>
 int launch_fd(const CUtensorMap& km, const CUtensorMap& vm, const __half* q, const int32_t* lens,
               __half* out, float* part, uint32_t* counters, int batch, int q_heads, int kv_heads,
               int max_seq, int kps, int splits, float scale_log2, cudaStream_t stream, bool pdl,
-              const int32_t* positions) {
+              const int32_t* positions, bool clustered) {
   auto kern = flash_decode_kernel<D, kWarps, kStages>;
   constexpr size_t smem = fd_smem_bytes<D>();
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -481,8 +528,9 @@ int launch_fd(const CUtensorMap& km, const CUtensorMap& vm, const __half* q, con
   cfg.smem = smem;
   cfg.stream = stream;
   cfg.pdl = pdl;
+  cfg.cluster = clustered ? splits : 1;
   return launch(cfg, kern, km, vm, q, lens, out, part, counters, q_heads, kv_heads, max_seq, kps,
-                splits, scale_log2, positions);
+                splits, scale_log2, positions, clustered ? 1 : 0);
 }
 
 }  // namespace
@@ -514,8 +562,20 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
   NPU_REQUIRE(num_splits >= 0 && num_splits <= kMaxSplits, "flash_decode: num_splits %d not in [0, %d]",
               num_splits, kMaxSplits);
   int kps = 0;
-  const int splits = resolve_splits(batch, kv_heads, max_seq, num_splits, &kps);
-  const size_t need = workspace_bytes_for(batch, kv_heads, head_dim, splits);
+  int splits = resolve_splits(batch, kv_heads, max_seq, num_splits, &kps);
+  // At most 4 (sequence, KV head) units (batch-1 decode of a tensor-parallel
+  // shard; the split count left to us): 8 splits per unit as one cluster,
+  // merged through distributed shared memory -- no workspace, no second
+  // round trip through L2.  With more units the cluster launch's wait for 8
+  // free SMs of one GPC behind the previous kernel costs more than it saves.
+  bool clustered = false;
+  if (num_splits == 0 && static_cast<long long>(batch) * kv_heads <= 4 && max_seq > kKeysPerTile) {
+    kps = (max_seq + 7) / 8;
+    kps = (kps + kKeysPerTile - 1) / kKeysPerTile * kKeysPerTile;
+    splits = (max_seq + kps - 1) / kps;
+    clustered = splits > 1;
+  }
+  const size_t need = clustered ? 0 : workspace_bytes_for(batch, kv_heads, head_dim, splits);
   NPU_REQUIRE(need == 0 || (workspace && workspace_bytes >= need),
               "flash_decode: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   NPU_REQUIRE(need == 0 || (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
@@ -538,9 +598,9 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
   __half* oh = static_cast<__half*>(out);
   if (head_dim == 128)
     return launch_fd<128>(km, vm, qh, seq_lens, oh, part, counters, batch, q_heads, kv_heads,
-                          max_seq, kps, splits, scale_log2, stream, pdl, positions);
+                          max_seq, kps, splits, scale_log2, stream, pdl, positions, clustered);
   return launch_fd<64>(km, vm, qh, seq_lens, oh, part, counters, batch, q_heads, kv_heads,
-                       max_seq, kps, splits, scale_log2, stream, pdl, positions);
+                       max_seq, kps, splits, scale_log2, stream, pdl, positions, clustered);
 }
 
 size_t flash_decode_workspace(int batch, int kv_heads, int head_dim, int max_seq, int num_splits) {

@@ -72,6 +72,29 @@ def test_ragged_and_empty_sequences(cuda):
         _check(got, ref)
 
 
+@pytest.mark.parametrize("batch,kv,dim,lens", [(1, 1, 128, [4096]), (2, 2, 128, [700, 0]),
+                                                (1, 4, 64, [333]), (4, 1, 128, [1, 31, 32, 1000])])
+def test_small_batch_cluster_merge(cuda, batch, kv, dim, lens):
+    """At most 4 (sequence, KV head) units with automatic splits: the splits of
+    a unit run as one thread-block cluster and merge through distributed shared
+    memory (ragged and empty sequences, garbage past each length)."""
+    group = 4
+    max_seq = max(max(lens), 64)
+    q = seeded((batch, kv * group, dim), 40 + batch)
+    k = seeded((batch, kv, max_seq, dim), 50 + kv)
+    v = seeded((batch, kv, max_seq, dim), 60 + dim)
+    for b, n in enumerate(lens):
+        k[b, :, n:] = float("nan")
+        v[b, :, n:] = float("inf")
+    ref = oracle.attention_decode(q, k, v, lens, dim ** -0.5)
+    got = _run(q, k, v, lens)
+    assert torch.isfinite(got).all()
+    for b, n in enumerate(lens):
+        if n == 0:
+            assert float(got[b].abs().max()) == 0.0
+    _check(got, ref)
+
+
 def test_sdpa_reference_cases(cuda):
     """The reference's SDPA cases with a supported head size, decode query row."""
     z = dict(np.load(GOLDEN / "sdpa_decode.npz"))
