@@ -57,18 +57,24 @@ __global__ void __launch_bounds__(kChunk)
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] +
         p.partial[static_cast<size_t>(b) * p.hidden + n];
   } else {
-    // Every rank's partial (tagged words, re-read until they have landed),
-    // added in rank order: the same bits on every rank.
+    // Every rank's partial (tagged words: all loads in flight at once, then
+    // late ones re-read until they have landed), added in rank order: the
+    // same bits on every rank.
     const uint32_t tag = px_tag(p.px, p.px.seq);
-    float part[kMaxRanks];
+    const size_t off = px_offset(p.px, b, n);
+    uint64_t w[kMaxRanks];
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-      part[r] = 0.f;
-      if (r < p.px.ranks) px_load(p.px, tag, r, b, n, &part[r]);
-    }
+    for (int r = 0; r < kMaxRanks; ++r) w[r] = r < p.px.ranks ? ld_relaxed_sys(p.px.part[r] + off) : 0;
     float sum = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) sum += part[r];
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < p.px.ranks) {
+        uint32_t bits = static_cast<uint32_t>(w[r]);
+        if (static_cast<uint32_t>(w[r] >> 32) != tag && !px_get(p.px.part[r] + off, tag, &bits))
+          bits = 0;
+        sum += __uint_as_float(bits);
+      }
+    }
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] + sum;
   }
   const float w = __half2float(p.norm_w[n]);
