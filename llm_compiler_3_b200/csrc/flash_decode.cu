@@ -588,7 +588,6 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
   rc = make_tensor_map_2d(&vm, v, rows, head_dim, kKeysPerTile, 64);
   if (rc) return rc;
 
-  const size_t units = static_cast<size_t>(batch) * kv_heads;
   uint32_t* counters = reinterpret_cast<uint32_t*>(workspace);
   float* part =
       need ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kCounterBytes)
