@@ -288,6 +288,17 @@ NPU_B200_API int npu_b200_set_weight(npu_b200_ctx* ctx, const char* name, const 
  * (python/npu/capture/export.py:30-40: arguments.txt + arg<N>.bin). */
 NPU_B200_API int npu_b200_load_capture(npu_b200_ctx* ctx, const char* capture_dir);
 
+/* Per-rank weight image: this rank's packed weight panels and norms (its
+ * tensor-parallel shard, already in the kernels' layout) as files under
+ * dir/rank<r>-of-<N>/ with a descriptor (image.txt: stage = cuda-image,
+ * schema = 1, the plan fingerprint, the rank, and per tensor its size and FNV-1a
+ * checksum).  Loading checks every stamp, size and checksum and copies the
+ * bytes as they are: no sharding, no packing.  The B200 counterpart of the
+ * reference's hbm.bin image (tools/npu-compile/npu-compile.cpp:495-659).  Saving
+ * needs every weight set; loading sets them all. */
+NPU_B200_API int npu_b200_save_image(npu_b200_ctx* ctx, const char* dir);
+NPU_B200_API int npu_b200_load_image(npu_b200_ctx* ctx, const char* dir);
+
 /* Device pointers of one layer's KV cache, each [max_batch][local kv heads][max_seq][head_dim]
  * FP16; sequence b's key at position p lives at [b][h][p][:]. */
 NPU_B200_API int npu_b200_kv_cache(npu_b200_ctx* ctx, int layer, void** d_k, void** d_v);

@@ -70,6 +70,8 @@ _SIGNATURES = [
     ("npu_b200_plan_check", c_int, [c_char_p, POINTER(c_int64), c_int]),
     ("npu_b200_set_weight", c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     ("npu_b200_load_capture", c_int, [c_void_p, c_char_p]),
+    ("npu_b200_save_image", c_int, [c_void_p, c_char_p]),
+    ("npu_b200_load_image", c_int, [c_void_p, c_char_p]),
     ("npu_b200_kv_cache", c_int, [c_void_p, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
     ("npu_b200_decode_step", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     ("npu_b200_decode_step_device", c_int,

@@ -30,6 +30,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <filesystem>
 #include <fstream>
 #include <map>
 #include <sstream>
@@ -1087,6 +1088,172 @@ extern "C" int npu_b200_load_capture(npu_b200_ctx* c, const char* dir) {
     ++used;
   }
   if (used == 0) return set_error(NPU_B200_E_PLAN, "%s names no weight of this plan", dir);
+  return NPU_B200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Per-rank weight image: this rank's packed panels and norms, saved as files
+// with a descriptor and read back without sharding or packing -- the B200
+// counterpart of the reference's hbm.bin image (tools/npu-compile/
+// npu-compile.cpp:495-659), whose stage stamps it keeps (stage, schema, the
+// plan fingerprint).
+// ---------------------------------------------------------------------------
+namespace npu_b200 {
+namespace {
+
+struct ImageEntry {
+  std::string name;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  std::vector<size_t> have;  // indices of c->have this tensor completes
+};
+
+std::vector<ImageEntry> image_entries(const npu_b200_ctx* c) {
+  const Plan& P = c->plan;
+  const int H = P.hidden, D = P.head_dim;
+  std::vector<ImageEntry> e;
+  for (int l = 0; l < P.layers; ++l) {
+    const LayerBuffers& L = c->layers[l];
+    const size_t base = static_cast<size_t>(l) * kPerLayerKinds;
+    const std::string pre = "layers." + std::to_string(l) + ".";
+    e.push_back({pre + "qkv", L.w_qkv, packed_weight_bytes((c->q_loc + 2 * c->kv_loc) * D, H),
+                 {base + kQ, base + kK, base + kV}});
+    e.push_back({pre + "o", L.w_o, packed_weight_bytes(H, c->q_loc * D), {base + kO}});
+    e.push_back({pre + "gate_up", L.w_gu, packed_weight_bytes(2 * c->ffn_loc, H),
+                 {base + kGate, base + kUp}});
+    e.push_back({pre + "down", L.w_down, packed_weight_bytes(H, c->ffn_loc), {base + kDown}});
+    e.push_back({pre + "input_layernorm", L.in_norm, static_cast<size_t>(H) * 2, {base + kInNorm}});
+    e.push_back({pre + "post_attention_layernorm", L.post_norm, static_cast<size_t>(H) * 2,
+                 {base + kPostNorm}});
+    if (P.qk_norm) {
+      e.push_back({pre + "q_norm", L.q_norm, static_cast<size_t>(D) * 2, {base + kQNorm}});
+      e.push_back({pre + "k_norm", L.k_norm, static_cast<size_t>(D) * 2, {base + kKNorm}});
+    }
+  }
+  if (P.vocab > 0) {
+    const size_t top = static_cast<size_t>(P.layers) * kPerLayerKinds;
+    e.push_back({"embed", c->embed, static_cast<size_t>(P.vocab) * H * 2, {top + 0}});
+    e.push_back({"final_norm", c->final_norm, static_cast<size_t>(H) * 2, {top + 1}});
+    e.push_back({"lm_head", c->lm_head, packed_weight_bytes(c->vocab_loc, H), {top + 2}});
+  }
+  return e;
+}
+
+uint64_t fnv1a_bytes(const uint8_t* p, size_t n) {
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < n; ++i) h = (h ^ p[i]) * 1099511628211ull;
+  return h;
+}
+
+std::string rank_dir(const npu_b200_ctx* c, const char* dir) {
+  return std::string(dir) + "/rank" + std::to_string(c->tp_rank) + "-of-" +
+         std::to_string(c->tp_size);
+}
+
+}  // namespace
+}  // namespace npu_b200
+
+extern "C" int npu_b200_save_image(npu_b200_ctx* c, const char* dir) {
+  clear_error();
+  NPU_REQUIRE(c && dir, "null argument");
+  if (!c->loaded) return set_error(NPU_B200_E_STATE, "no plan loaded");
+  std::string missing;
+  if (required_missing(c, c->plan.vocab > 0, &missing))
+    return set_error(NPU_B200_E_STATE, "image: weight %s was never set", missing.c_str());
+  NPU_TRY_CUDA(cudaSetDevice(c->device));
+  NPU_TRY_CUDA(cudaDeviceSynchronize());
+  const std::string root = rank_dir(c, dir);
+  std::error_code ec;
+  std::filesystem::create_directories(root, ec);
+  if (ec) return set_error(NPU_B200_E_INVALID, "image: cannot create %s", root.c_str());
+  std::ostringstream desc;
+  desc << "stage = cuda-image\nschema = 1\nfingerprint = " << c->plan.fingerprint
+       << "\ntp_rank = " << c->tp_rank << "\ntp_size = " << c->tp_size << "\n";
+  std::vector<uint8_t> host;
+  for (const ImageEntry& t : image_entries(c)) {
+    host.resize(t.bytes);
+    NPU_TRY_CUDA(cudaMemcpy(host.data(), t.ptr, t.bytes, cudaMemcpyDeviceToHost));
+    const std::string file = t.name + ".bin";
+    std::ofstream out(root + "/" + file, std::ios::binary | std::ios::trunc);
+    out.write(reinterpret_cast<const char*>(host.data()), static_cast<std::streamsize>(t.bytes));
+    if (!out) return set_error(NPU_B200_E_INVALID, "image: cannot write %s/%s", root.c_str(), file.c_str());
+    char sum[32];
+    snprintf(sum, sizeof(sum), "%016llx", static_cast<unsigned long long>(fnv1a_bytes(host.data(), t.bytes)));
+    desc << "tensor " << t.name << " " << t.bytes << " " << sum << " " << file << "\n";
+  }
+  std::ofstream d(root + "/image.txt", std::ios::trunc);
+  d << desc.str();
+  if (!d) return set_error(NPU_B200_E_INVALID, "image: cannot write %s/image.txt", root.c_str());
+  return NPU_B200_OK;
+}
+
+extern "C" int npu_b200_load_image(npu_b200_ctx* c, const char* dir) {
+  clear_error();
+  NPU_REQUIRE(c && dir, "null argument");
+  if (!c->loaded) return set_error(NPU_B200_E_STATE, "no plan loaded");
+  NPU_TRY_CUDA(cudaSetDevice(c->device));
+  const std::string root = rank_dir(c, dir);
+  std::ifstream in(root + "/image.txt");
+  if (!in) return set_error(NPU_B200_E_PLAN, "image: cannot read %s/image.txt", root.c_str());
+  std::map<std::string, std::string> keys;
+  std::map<std::string, std::vector<std::string>> tensors;
+  std::string line;
+  while (std::getline(in, line)) {
+    std::istringstream ls(line);
+    std::string first;
+    if (!(ls >> first)) continue;
+    if (first == "tensor") {
+      std::string name, bytes, sum, file;
+      if (!(ls >> name >> bytes >> sum >> file))
+        return set_error(NPU_B200_E_PLAN, "image: malformed line '%s'", line.c_str());
+      if (tensors.count(name)) return set_error(NPU_B200_E_PLAN, "image: duplicate tensor %s", name.c_str());
+      tensors[name] = {bytes, sum, file};
+    } else {
+      std::string eq, value;
+      if (!(ls >> eq >> value) || eq != "=")
+        return set_error(NPU_B200_E_PLAN, "image: malformed line '%s'", line.c_str());
+      keys[first] = value;
+    }
+  }
+  if (keys["stage"] != "cuda-image" || keys["schema"] != "1")
+    return set_error(NPU_B200_E_PLAN, "image: stage '%s' schema '%s', expected cuda-image 1",
+                     keys["stage"].c_str(), keys["schema"].c_str());
+  if (keys["fingerprint"] != std::to_string(c->plan.fingerprint))
+    return set_error(NPU_B200_E_PLAN, "image: made for another plan (fingerprint %s, plan %llu)",
+                     keys["fingerprint"].c_str(), static_cast<unsigned long long>(c->plan.fingerprint));
+  if (keys["tp_rank"] != std::to_string(c->tp_rank) || keys["tp_size"] != std::to_string(c->tp_size))
+    return set_error(NPU_B200_E_PLAN, "image: made for rank %s of %s", keys["tp_rank"].c_str(),
+                     keys["tp_size"].c_str());
+  const std::vector<ImageEntry> want = image_entries(c);
+  if (tensors.size() != want.size())
+    return set_error(NPU_B200_E_PLAN, "image: %zu tensors, the plan needs %zu", tensors.size(),
+                     want.size());
+  std::vector<uint8_t> host;
+  for (const ImageEntry& t : want) {
+    auto it = tensors.find(t.name);
+    if (it == tensors.end()) return set_error(NPU_B200_E_PLAN, "image: no tensor %s", t.name.c_str());
+    const std::vector<std::string>& f = it->second;
+    if (f[0] != std::to_string(t.bytes))
+      return set_error(NPU_B200_E_PLAN, "image: %s has %s bytes, the plan needs %zu", t.name.c_str(),
+                       f[0].c_str(), t.bytes);
+    if (f[2].find('/') != std::string::npos || f[2].find("..") != std::string::npos)
+      return set_error(NPU_B200_E_PLAN, "image: file name '%s' leaves the image", f[2].c_str());
+    std::ifstream bin(root + "/" + f[2], std::ios::binary | std::ios::ate);
+    if (!bin || static_cast<size_t>(bin.tellg()) != t.bytes)
+      return set_error(NPU_B200_E_PLAN, "image: %s/%s is missing or not %zu bytes", root.c_str(),
+                       f[2].c_str(), t.bytes);
+    bin.seekg(0);
+    host.resize(t.bytes);
+    if (!bin.read(reinterpret_cast<char*>(host.data()), static_cast<std::streamsize>(t.bytes)))
+      return set_error(NPU_B200_E_PLAN, "image: short read of %s", f[2].c_str());
+    char sum[32];
+    snprintf(sum, sizeof(sum), "%016llx", static_cast<unsigned long long>(fnv1a_bytes(host.data(), t.bytes)));
+    if (f[1] != sum)
+      return set_error(NPU_B200_E_PLAN, "image: %s checksum %s, the descriptor says %s",
+                       t.name.c_str(), sum, f[1].c_str());
+    NPU_TRY_CUDA(cudaMemcpy(t.ptr, host.data(), t.bytes, cudaMemcpyHostToDevice));
+    for (size_t h : t.have) c->have[h] = 1;
+  }
   return NPU_B200_OK;
 }
 

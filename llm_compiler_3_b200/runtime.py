@@ -75,6 +75,14 @@ class Decoder:
         for name, t in items:
             self.set_weight(name, t)
 
+    def save_image(self, directory: str | Path) -> None:
+        """This rank's weights as a per-rank image under directory/rank<r>-of-<N>/."""
+        _native.check(self.lib.npu_b200_save_image(self._ctx, str(directory).encode()))
+
+    def load_image(self, directory: str | Path) -> None:
+        """Every weight from a per-rank image written by save_image for this plan and rank."""
+        _native.check(self.lib.npu_b200_load_image(self._ctx, str(directory).encode()))
+
     def load_capture(self, directory: str | Path) -> None:
         """Every weight of a capture directory (arguments.txt + arg<N>.bin)."""
         _native.check(self.lib.npu_b200_load_capture(self._ctx, str(directory).encode()))
