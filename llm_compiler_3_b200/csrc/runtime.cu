@@ -1,5 +1,6 @@
 // Decode runtime: plan, per-rank weights and KV cache, one CUDA graph per
-// (mode, batch), NCCL tensor parallelism.
+// (mode, batch), tensor parallelism over NVLink peer memory (NCCL for setup,
+// and as the fallback exchange).
 //
 // This is the B200 counterpart of what LLM_Compiler_3 does after its front
 // end: where the reference tiles, places, lowers and encodes the legalized graph
@@ -13,14 +14,17 @@
 //   residual_update(embed)                      h, xw = h*w_in, ssq
 //   per layer:  proj[QKV: rms scale, (QK-norm), RoPE, KV append]
 //               flash_decode (split-KV, GQA group per CTA)
-//               proj[O: + residual, xw = h*w_post, ssq]        (TP: -> all-reduce)
+//               proj[O: + residual, xw = h*w_post, ssq]        (TP: all-reduce first)
 //               proj[gate|up: rms scale, SwiGLU]
-//               proj[down: + residual, xw = h*w_next, ssq]     (TP: -> all-reduce)
-//   proj[LM head: rms scale, per-tile argmax] -> argmax_reduce (TP: all-gather)
+//               proj[down: + residual, xw = h*w_next, ssq]     (TP: all-reduce first)
+//   proj[LM head: rms scale, per-tile argmax] -> argmax_reduce (TP: gather over ranks)
 //
 // At batch 1-2 every proj runs as the CUDA-core GEMV (gemv.cu) and the sums of
 // squares and partial argmaxes are kept per 16 rows; above, on the tensor
-// cores with per-128-row partials.
+// cores with per-128-row partials.  With tensor parallelism the all-reduce is
+// the exchange of peer.cuh: at batch 1-2 inside the GEMV's residual epilogue,
+// above it in residual_update after a STORE projection (NCCL all-reduce when
+// peer memory is unavailable).
 // Every kernel is launched with programmatic dependent launch, so the next
 // projection starts streaming its weights while the previous kernel drains.
 #include <dlfcn.h>
@@ -825,7 +829,7 @@ int finish_argmax(npu_b200_ctx* c, int batch, cudaStream_t s) {
   if (c->px_ready) {
     PeerExchange x = c->px;
     x.seq = kArgmaxSeq;
-    if ((rc = argmax_reduce_push(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch,
+    if ((rc = argmax_reduce_publish(c->am_val, c->am_idx, lm_tiles, P.max_batch, batch,
                                  c->vocab_off, x, s, true)))
       return rc;
     return argmax_combine_peers(x, batch, c->d_ids, s, true);

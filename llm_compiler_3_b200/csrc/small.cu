@@ -9,7 +9,7 @@
 //  * argmax_reduce / argmax_combine: greedy token choice over the per-tile
 //    (max, index) pairs the LM-head epilogue leaves, ties to the lowest id;
 //    with tensor parallelism the per-rank results go through NCCL or, over
-//    peer memory, argmax_reduce_push / argmax_combine_peers.
+//    peer memory, argmax_reduce_publish / argmax_combine_peers.
 //  * store_hidden: FP32 residual -> FP16 hidden-state output.
 #include <math.h>
 
@@ -104,92 +104,77 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
+// Token blockIdx.x's (max, index) over n_tiles partials (part[t * ld + b]),
+// lowest index on ties; thread 0's *bv_out / *bi_out hold the result.
+__device__ __forceinline__ void block_argmax(const float* __restrict__ part_val,
+                                             const int32_t* __restrict__ part_idx, int n_tiles,
+                                             int ld, float* bv_out, int* bi_out) {
+  const int b = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
+    const float v = part_val[static_cast<size_t>(t) * ld + b];
+    const int i = part_idx[static_cast<size_t>(t) * ld + b];
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+  }
+  *bv_out = bv;
+  *bi_out = bi;
+}
+
 __global__ void __launch_bounds__(256)
     argmax_reduce_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
                          int n_tiles, int ld, int id_offset, float* __restrict__ out_val,
                          int32_t* __restrict__ out_idx) {
   pdl_launch_dependents();
   pdl_wait();
-  const int b = blockIdx.x;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
-    const float v = part_val[static_cast<size_t>(t) * ld + b];
-    const int i = part_idx[static_cast<size_t>(t) * ld + b];
-    if (better(v, i, bv, bi)) {
-      bv = v;
-      bi = i;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (better(ov, oi, bv, bi)) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  __shared__ float sv[8];
-  __shared__ int si[8];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    sv[warp] = bv;
-    si[warp] = bi;
-  }
-  __syncthreads();
+  float bv;
+  int bi;
+  block_argmax(part_val, part_idx, n_tiles, ld, &bv, &bi);
   if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-      if (better(sv[w], si[w], bv, bi)) {
-        bv = sv[w];
-        bi = si[w];
-      }
-    out_val[b] = bv;
-    out_idx[b] = bi + id_offset;
+    out_val[blockIdx.x] = bv;
+    out_idx[blockIdx.x] = bi + id_offset;
   }
 }
 
+// The same, published as tagged words in this rank's exchange buffer.
 __global__ void __launch_bounds__(256)
-    argmax_push_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
-                       int n_tiles, int ld, int id_offset, const PeerExchange px) {
+    argmax_publish_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
+                          int n_tiles, int ld, int id_offset, const PeerExchange px) {
   pdl_launch_dependents();
   pdl_wait();
-  const int b = blockIdx.x;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
-    const float v = part_val[static_cast<size_t>(t) * ld + b];
-    const int i = part_idx[static_cast<size_t>(t) * ld + b];
-    if (better(v, i, bv, bi)) {
-      bv = v;
-      bi = i;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (better(ov, oi, bv, bi)) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  __shared__ float sv[8];
-  __shared__ int si[8];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    sv[warp] = bv;
-    si[warp] = bi;
-  }
-  __syncthreads();
+  float bv;
+  int bi;
+  block_argmax(part_val, part_idx, n_tiles, ld, &bv, &bi);
   if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-      if (better(sv[w], si[w], bv, bi)) {
-        bv = sv[w];
-        bi = si[w];
-      }
     const uint32_t tag = px_tag(px, kArgmaxSeq);
-    uint64_t* w = px.part[px.rank] + px_argmax_offset(px, b);
+    uint64_t* w = px.part[px.rank] + px_argmax_offset(px, blockIdx.x);
     px_put(w, tag, __float_as_uint(bv));
     px_put(w + 1, tag, static_cast<uint32_t>(bi + id_offset));
   }
@@ -275,7 +260,7 @@ int argmax_reduce(const float* part_val, const int32_t* part_idx, int n_tiles, i
                 out_idx);
 }
 
-int argmax_reduce_push(const float* part_val, const int32_t* part_idx, int n_tiles, int ld,
+int argmax_reduce_publish(const float* part_val, const int32_t* part_idx, int n_tiles, int ld,
                        int batch, int id_offset, const PeerExchange& px, cudaStream_t stream,
                        bool pdl) {
   NPU_REQUIRE(px.ranks >= 1 && px.ranks <= kMaxRanks && batch <= px.max_batch,
@@ -285,7 +270,7 @@ int argmax_reduce_push(const float* part_val, const int32_t* part_idx, int n_til
   cfg.block = dim3(256);
   cfg.stream = stream;
   cfg.pdl = pdl;
-  return launch(cfg, argmax_push_kernel, part_val, part_idx, n_tiles, ld, id_offset, px);
+  return launch(cfg, argmax_publish_kernel, part_val, part_idx, n_tiles, ld, id_offset, px);
 }
 
 int argmax_combine_peers(const PeerExchange& px, int batch, int32_t* out_ids, cudaStream_t stream,

@@ -13,7 +13,7 @@ enum ResidualSource : int {
   kResidFromEmbedding = 0,  // h = embed[tokens[b]]
   kResidFromHidden = 1,     // h = hidden_in[b] (FP16)
   kResidAddPartial = 2,     // h = resid[b] + partial[b] (after the all-reduce), or
-                            // resid[b] + the ranks' pushed partials in rank order (px)
+                            // resid[b] + every rank's published partial in rank order (px)
 };
 
 struct ResidualUpdate {
@@ -48,7 +48,7 @@ int argmax_combine(const float* gathered, int ranks, int ld, int batch, int32_t*
 // as tagged words in its exchange buffer (px; seq is ignored); the combine
 // reads every rank's pair over NVLink once it has landed and keeps the largest
 // value, lowest id on ties.
-int argmax_reduce_push(const float* part_val, const int32_t* part_idx, int n_tiles, int ld,
+int argmax_reduce_publish(const float* part_val, const int32_t* part_idx, int n_tiles, int ld,
                        int batch, int id_offset, const PeerExchange& px, cudaStream_t stream,
                        bool pdl);
 int argmax_combine_peers(const PeerExchange& px, int batch, int32_t* out_ids, cudaStream_t stream,
