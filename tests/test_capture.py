@@ -131,3 +131,52 @@ def test_runtime_runs_capture_directory(cuda, tmp_path, family):
     for b, p in enumerate(z["positions"].tolist()):
         assert float((k_after[b, :, p].float() - want_k[b, :, p]).abs().max()) <= 2e-2
         assert float((v_after[b, :, p].float() - want_v[b, :, p]).abs().max()) <= 2e-2
+
+
+def test_plan_from_capture_block(tmp_path):
+    """The plan read off a captured block's argument shapes (and its lifted
+    inv_freq buffer) is the plan of the layer's config."""
+    from llm_compiler_3_b200.capture import write_decode_capture
+    from llm_compiler_3_b200.plan import DecodePlan, plan_from_capture
+    step, config, z = _step("qwen3")
+    write_decode_capture(step, config, _inputs(z), tmp_path)
+    got = plan_from_capture(tmp_path, max_batch=2, max_seq=48)
+    want = DecodePlan.from_hf_config(config, max_batch=2, max_seq=48, layers=1, with_vocab=False)
+    assert got.text() == want.text()
+
+
+def test_plan_from_capture_stack_cli(tmp_path):
+    """A whole-model capture (layers.<i>. names, embedding, RoPE buffer): layer
+    count, vocabulary and the exact inverse frequencies; the CLI's plan parses
+    with the library's own checks."""
+    import ctypes
+    from llm_compiler_3_b200 import _native
+    from llm_compiler_3_b200.plan import main, plan_from_capture, rope_inv_freq
+    H, F, V, D = 512, 1024, 1000, 128
+    shapes = {"self_attn.q_proj.weight": (4 * D, H), "self_attn.k_proj.weight": (2 * D, H),
+              "self_attn.v_proj.weight": (2 * D, H), "self_attn.o_proj.weight": (H, 4 * D),
+              "mlp.gate_proj.weight": (F, H), "mlp.up_proj.weight": (F, H),
+              "mlp.down_proj.weight": (H, F), "input_layernorm.weight": (H,),
+              "post_attention_layernorm.weight": (H,)}
+    names = {"model.embed_tokens.weight": (V, H), "model.norm.weight": (H,),
+             "lm_head.weight": (V, H), "model.rotary_emb.inv_freq": (D // 2,)}
+    for layer in range(3):
+        for name, shape in shapes.items():
+            names[f"model.layers.{layer}.{name}"] = shape
+    lines = ["0 input0 1x7 int64"]
+    for i, name in enumerate(sorted(names), start=1):
+        dtype = "float32" if name.endswith("inv_freq") else "float16"
+        lines.append(f"{i} {name} {'x'.join(map(str, names[name]))} {dtype}")
+        if name.endswith("inv_freq"):
+            inv = np.asarray(rope_inv_freq(250000.0, D), dtype="<f4")
+            (tmp_path / f"arg{i}.bin").write_bytes(inv.tobytes())
+    (tmp_path / "arguments.txt").write_text("\n".join(lines) + "\n")
+    plan = plan_from_capture(tmp_path, max_batch=8, max_seq=512)
+    assert (plan.layers, plan.hidden, plan.heads, plan.kv_heads, plan.ffn, plan.vocab) == \
+        (3, H, 4, 2, F, V)
+    assert plan.arch == "llama" and plan.inv_freq == rope_inv_freq(250000.0, D)
+    assert abs(plan.rope_theta - 250000.0) / 250000.0 < 1e-4
+    assert main(["--from-capture", str(tmp_path), "--max-batch", "8", "--max-seq", "512"]) == 0
+    info = (ctypes.c_int64 * 12)()
+    _native.check(_native.lib().npu_b200_plan_check(str(tmp_path / "plan.txt").encode(), info, 12))
+    assert list(info)[:6] == [3, H, 4, 2, F, V]
