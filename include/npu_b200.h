@@ -123,6 +123,29 @@ NPU_B200_API int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k,
                                                int max_seq, float scale, int num_splits,
                                                void* stream);
 
+/* Multi-query (prefill) attention on tcgen05 tensor cores.
+ *
+ * Replaces the NPU lowering of npu.attention with M >= 1 queries per head and
+ * of its causal form (lib/Transforms/Attention.cpp:187-375; the is_causal mask as
+ * recognised at 70-92, blocks past the diagonal skipped at 221-222): per query
+ * head h with KV head h / group,
+ *   out[b,h,i] = sum_j softmax_j(scale * q[b,h,i] . k[b,h/group,j]) v[b,h/group,j]
+ * over keys j < keys and, when causal != 0, j <= q_start[b] + i (d_q_start NULL:
+ * 0, torch's top-left is_causal mask).  FP32 scores, online softmax and
+ * accumulation; the softmax weights are rounded to FP16 as the second MMA's
+ * operand; the output is rounded once.  A row that sees no key is zero.
+ *
+ *   d_q, d_out [batch, q_heads, queries, head_dim]
+ *   d_k, d_v   [batch, kv_heads, max_seq, head_dim]   (the KV-cache layout)
+ *   d_q_start  [batch] int32 or NULL
+ *   head_dim in {32, 64, 128}; keys in [0, max_seq]; batch x kv_heads <= 65535;
+ *   every pointer 16-byte aligned.  No workspace; calls may overlap. */
+NPU_B200_API int npu_b200_prefill_attention(const void* d_q, const void* d_k, const void* d_v,
+                                            const int32_t* d_q_start, void* d_out, int batch,
+                                            int q_heads, int kv_heads, int head_dim, int queries,
+                                            int keys, int max_seq, float scale, int causal,
+                                            void* stream);
+
 /* Linear layer on tcgen05 tensor cores:
  *   out[b, n] = act( sum_k x[b, k] * w[n, k] + bias[n] ),  FP32 accumulation.
  *

@@ -52,6 +52,9 @@ _SIGNATURES = [
     ("npu_b200_flash_decode_noalloc", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
       c_float, c_int, c_void_p]),
+    ("npu_b200_prefill_attention", c_int,
+     [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+      c_int, c_int, c_float, c_int, c_void_p]),
     ("npu_b200_linear_workspace_size", c_size_t, [c_int, c_int, c_int]),
     ("npu_b200_linear", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t,

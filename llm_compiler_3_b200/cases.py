@@ -7,6 +7,7 @@ more to skip the cold first launch.
 
     python -m llm_compiler_3_b200.cases proj --rows 4096 --k 14336 --batch 1
     python -m llm_compiler_3_b200.cases flash --batch 64 --seq 4096
+    python -m llm_compiler_3_b200.cases prefill --queries 4096 --sdpa
     python -m llm_compiler_3_b200.cases step --batch 1 --layers 32 --seq 4096
 """
 from __future__ import annotations
@@ -76,6 +77,33 @@ def case_flash(a) -> str:
     return f"flash batch={a.batch} seq={a.seq}: {us:.1f} us/launch, {gbs:.0f} GB/s K+V"
 
 
+def case_prefill(a) -> str:
+    """Causal attention of a `queries`-token prompt appended after `prefix` cached
+    tokens (every sequence alike), head size 128; FLOPs count visible keys only.
+    With --sdpa (prefix 0) also times torch's SDPA on the same tensors."""
+    import torch
+    from . import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    keys = a.prefix + a.queries
+    q = torch.randn(a.batch, a.q_heads, a.queries, 128, device=dev, generator=g).half()
+    k = torch.randn(a.batch, a.kv_heads, keys, 128, device=dev, generator=g).half()
+    v = torch.randn(a.batch, a.kv_heads, keys, 128, device=dev, generator=g).half()
+    start = torch.full((a.batch,), a.prefix, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    us = _timed(lambda: ops.prefill_attention(q, k, v, keys=keys, q_start=start, causal=True,
+                                              out=out), a.repeat, a.graph)
+    visible = sum(min(a.prefix + i + 1, keys) for i in range(a.queries))
+    flops = 4.0 * 128 * visible * a.batch * a.q_heads
+    line = (f"prefill batch={a.batch} queries={a.queries} prefix={a.prefix}: {us:.1f} us/launch, "
+            f"{flops / us / 1e6:.0f} TFLOP/s")
+    if a.sdpa and a.prefix == 0:
+        f = torch.nn.functional.scaled_dot_product_attention
+        ref = _timed(lambda: f(q, k, v, is_causal=True, enable_gqa=True), a.repeat, a.graph)
+        line += f"; torch SDPA {ref:.1f} us/launch, {flops / ref / 1e6:.0f} TFLOP/s"
+    return line
+
+
 def case_step(a) -> str:
     """Greedy decode steps of the Llama-3-8B-shaped stack (random weights,
     cache filled to seq - 1, position seq - 1), one CUDA graph per step."""
@@ -136,13 +164,23 @@ def main(argv=None) -> int:
     f.add_argument("--seq", type=int, default=4096)
     f.add_argument("--repeat", type=int, default=3)
     f.add_argument("--graph", action="store_true", help="time graph replays of the launches")
+    r = sub.add_parser("prefill")
+    r.add_argument("--batch", type=int, default=1)
+    r.add_argument("--q-heads", type=int, default=32)
+    r.add_argument("--kv-heads", type=int, default=8)
+    r.add_argument("--queries", type=int, default=4096)
+    r.add_argument("--prefix", type=int, default=0)
+    r.add_argument("--repeat", type=int, default=5)
+    r.add_argument("--graph", action="store_true", help="time graph replays of the launches")
+    r.add_argument("--sdpa", action="store_true", help="also time torch SDPA (prefix 0)")
     s = sub.add_parser("step")
     s.add_argument("--batch", type=int, default=1)
     s.add_argument("--layers", type=int, default=32)
     s.add_argument("--seq", type=int, default=4096)
     s.add_argument("--repeat", type=int, default=5)
     a = ap.parse_args(argv)
-    print({"proj": case_proj, "flash": case_flash, "step": case_step}[a.case](a), flush=True)
+    cases = {"proj": case_proj, "flash": case_flash, "prefill": case_prefill, "step": case_step}
+    print(cases[a.case](a), flush=True)
     return 0
 
 

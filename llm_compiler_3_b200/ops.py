@@ -79,6 +79,43 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return out
 
 
+def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      keys: int | None = None, q_start: torch.Tensor | None = None,
+                      causal: bool = False, scale: float | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Multi-query attention on tcgen05: q [B, Hq, M, D], caches [B, Hkv, S, D].
+
+    out[b, h, i] = softmax(scale q K^T) V over keys j < keys (default S) and, when
+    causal, j <= q_start[b] + i (q_start [B] int32, default 0: torch's is_causal).
+    Returns out [B, Hq, M, D] FP16; a row that sees no key is zero."""
+    _require(q, "q", ndim=4)
+    _require(k_cache, "k_cache", ndim=4)
+    _require(v_cache, "v_cache", ndim=4)
+    batch, q_heads, queries, head_dim = q.shape
+    _, kv_heads, max_seq, d2 = k_cache.shape
+    if v_cache.shape != k_cache.shape or d2 != head_dim or k_cache.shape[0] != batch:
+        raise ValueError("k_cache / v_cache / q shapes disagree")
+    if q_start is not None:
+        _require(q_start, "q_start", dtype=torch.int32, ndim=1)
+        if q_start.shape[0] != batch:
+            raise ValueError("q_start must have one entry per sequence")
+    if keys is None:
+        keys = max_seq
+    if scale is None:
+        scale = head_dim ** -0.5
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _require(out, "out", ndim=4)
+        if out.shape != q.shape:
+            raise ValueError("out must have q's shape")
+    _native.check(_native.lib().npu_b200_prefill_attention(
+        _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(q_start), _ptr(out), batch, q_heads,
+        kv_heads, head_dim, queries, int(keys), max_seq, float(scale), 1 if causal else 0,
+        _stream()))
+    return out
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            relu: bool = False, out_dtype: torch.dtype = torch.float16,
            out: torch.Tensor | None = None) -> torch.Tensor:

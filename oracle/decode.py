@@ -37,7 +37,7 @@ import torch
 
 __all__ = [
     "DecoderShape", "grid_values", "linear", "rms_norm", "rope_inv_freq", "rope_cos_sin",
-    "apply_rope", "attention_decode", "attention_online", "silu_mul", "decoder_layer_decode",
+    "apply_rope", "attention_decode", "attention_prefill", "attention_online", "silu_mul", "decoder_layer_decode",
     "stack_decode", "mlp_forward", "greedy_argmax", "cosine", "LLAMA3_8B", "QWEN3_8B",
 ]
 
@@ -138,6 +138,38 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         scores = torch.einsum("kgd,knd->kgn", qg, k) * scale
         probs = torch.softmax(scores, dim=-1)
         out[b] = torch.einsum("kgn,knd->kgd", probs, v).reshape(heads, dim)
+    return out
+
+
+def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      keys: int, scale: float, causal: bool, q_start=None) -> torch.Tensor:
+    """M queries per head against keys [0, keys) of the cache: npu.attention with
+    M >= 1 rows (NPUDialect.td:31-61).  Causal: query i of sequence b sees key j
+    iff j <= q_start[b] + i; q_start 0 is the mask the frontend builds for
+    is_causal (0 where the key index is at most the query index, -inf elsewhere,
+    Attention.cpp:70-92).  A row with no visible key yields zeros.
+
+    q [B, Hq, M, D]; k_cache, v_cache [B, Hkv, S, D]; returns FP32 [B, Hq, M, D]."""
+    batch, heads, queries, dim = q.shape
+    kv_heads = k_cache.shape[1]
+    group = heads // kv_heads
+    out = torch.zeros(batch, heads, queries, dim, dtype=torch.float32)
+    if keys <= 0:
+        return out
+    for b in range(batch):
+        k = _f32(k_cache[b, :, :keys]).repeat_interleave(group, dim=0)   # [Hq, n, D]
+        v = _f32(v_cache[b, :, :keys]).repeat_interleave(group, dim=0)
+        scores = torch.einsum("hmd,hnd->hmn", _f32(q[b]), k) * scale
+        if causal:
+            start = 0 if q_start is None else int(q_start[b])
+            rows = torch.arange(queries)[:, None] + start
+            visible = torch.arange(keys)[None, :] <= rows
+            scores = scores.masked_fill(~visible, float("-inf"))
+            seen = visible.any(dim=1)
+        else:
+            seen = torch.ones(queries, dtype=torch.bool)
+        probs = torch.softmax(scores, dim=-1).nan_to_num(0.0) * seen[None, :, None]
+        out[b] = torch.einsum("hmn,hnd->hmd", probs, v)
     return out
 
 
