@@ -86,6 +86,31 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64
   return NPU_B200_OK;
 }
 
+int make_tensor_map_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                       uint64_t planes, uint64_t plane_bytes, uint32_t box_rows,
+                       uint32_t box_cols) {
+  CUtensorMap probe;
+  int rc = make_tensor_map_2d(&probe, base, 1, cols, 1, box_cols);  // loads the encoder, checks base/pitch
+  if (rc) return rc;
+  if (plane_bytes % 16 != 0 || plane_bytes < rows * cols * 2)
+    return set_error(NPU_B200_E_INVALID, "plane pitch %llu B is not a multiple of 16 or too small",
+                     static_cast<unsigned long long>(plane_bytes));
+  if (box_rows > 256 || box_rows == 0 || rows == 0 || planes == 0)
+    return set_error(NPU_B200_E_INVALID, "bad 3-D TMA box %u rows over %llu x %llu", box_rows,
+                     static_cast<unsigned long long>(rows), static_cast<unsigned long long>(planes));
+  cuuint64_t dims[3] = {cols, rows, planes};
+  cuuint64_t strides[2] = {cols * 2, plane_bytes};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NPU_B200_E_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", static_cast<int>(r));
+  return NPU_B200_OK;
+}
+
 }  // namespace npu_b200
 
 using namespace npu_b200;

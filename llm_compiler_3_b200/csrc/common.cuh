@@ -110,6 +110,44 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_
   return false;
 }
 
+// Non-suspending test of one mbarrier phase.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Spinning form of wait_or_abort for a single latency-critical thread (it
+// reacts to the phase completing without the suspend of try_wait); bounded by
+// 16 x kMaxPolls tests.
+__device__ __forceinline__ bool spin_or_abort(uint64_t* bar, uint32_t phase,
+                                              const volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kMaxPolls * 16u; ++i) {
+    if (mbar_test_wait(bar, phase)) return true;
+    if ((i & 63u) == 63u && *abort_flag) return false;
+  }
+  report_error(kDevErrTmaTimeout);
+  return false;
+}
+
+// Bounded wait that also gives up as soon as another warp raised the abort
+// flag; only running out of polls is reported as a device error.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase,
+                                              const volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (*abort_flag) return false;
+  }
+  report_error(kDevErrTmaTimeout);
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tensor and plain bulk copies), global -> shared, completion on mbarrier
 // ---------------------------------------------------------------------------
@@ -119,6 +157,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 3-D tiled load: coordinates (x innermost, y, z).
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -275,6 +323,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Two base-2 exponentials of an FP16 pair (PTX ex2.approx.f16x2).
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05 (5th-generation tensor cores, accumulators in tensor memory)
 // ---------------------------------------------------------------------------
@@ -309,6 +364,19 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t desc_a, uin
       : "memory");
 }
 
+// One tcgen05.mma, kind::f16, A from tensor memory (row i in lane i, two FP16
+// per 32-bit column, 8 columns per 16-wide k-step), B from a shared-memory
+// descriptor.
+__device__ __forceinline__ void tc_mma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread
 // have completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -331,6 +399,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 32 bits, 16 consecutive columns per thread, register -> TMEM.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand stored with the
 // 128-byte swizzle TMA writes: 8-row atoms of 128 B, atoms 1024 B apart.
@@ -343,6 +423,24 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   d |= static_cast<uint64_t>(2u) << 61;                            // layout: SWIZZLE_128B
   return d;
 }
+
+// Shared-memory matrix descriptor for an MN-major operand stored as TMA tiles
+// with the 128-byte swizzle: rows of 64 MN-contiguous elements (128 B), 8-row
+// groups along K `k_group_bytes` apart, 64-element MN blocks `mn_block_bytes`
+// apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t smem_addr, uint32_t mn_block_bytes,
+                                                       uint32_t k_group_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);                // start address
+  d |= static_cast<uint64_t>((mn_block_bytes >> 4) & 0x3FFFu) << 16;     // LBO: MN blocks
+  d |= static_cast<uint64_t>((k_group_bytes >> 4) & 0x3FFFu) << 32;      // SBO: 8-row K groups
+  d |= static_cast<uint64_t>(1u) << 46;                                  // descriptor version
+  d |= static_cast<uint64_t>(2u) << 61;                                  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor bit: the B operand is MN-major (N contiguous).
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
 
 // Instruction descriptor, kind::f16: fp16 A/B (K-major), fp32 accumulate.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {

@@ -41,18 +41,6 @@ __device__ __forceinline__ bool consumer_sync_or(bool pred) {
   return any != 0;
 }
 
-// Bounded wait that also gives up as soon as another warp raised the abort
-// flag; only running out of polls is reported as a device error.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase,
-                                              const volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
-    if (mbar_try_wait(bar, phase)) return true;
-    if (*abort_flag) return false;
-  }
-  report_error(kDevErrTmaTimeout);
-  return false;
-}
-
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }

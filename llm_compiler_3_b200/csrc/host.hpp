@@ -38,6 +38,13 @@ int sm_count();
 int make_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                        uint32_t box_rows, uint32_t box_cols);
 
+// 3-D tensor map over `planes` row-major FP16 matrices [rows, cols], plane_bytes
+// apart, box box_cols x box_rows x 1, 128-byte swizzle.  Elements past `rows`
+// in a plane (or past the last plane) load as zero.
+int make_tensor_map_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                       uint64_t planes, uint64_t plane_bytes, uint32_t box_rows,
+                       uint32_t box_cols);
+
 // Launch helper: enables programmatic dependent launch when `pdl` is set.
 struct LaunchCfg {
   dim3 grid, block;

@@ -350,6 +350,426 @@ int launch_pa(const __half* q, const __half* k, const __half* v, const int32_t* 
                 hp, q_blocks, scale_log2, causal);
 }
 
+// ---------------------------------------------------------------------------
+// Head size 128 (scale > 0): two query tiles per CTA on a warp-specialised
+// pipeline.
+//
+//   warps 0-3  softmax of query tile 0 (thread r: row r, TMEM lane r)
+//   warps 4-7  softmax of query tile 1
+//   warp  8    TMA producer: both Q tiles once, then 64-key K and V tiles into
+//              3-stage rings (3-D tensor maps whose row extent is `keys`, so
+//              keys past it load as zero)
+//   warp  9    MMA issuer (one thread) and TMEM owner
+// Tensor-pipe order per key tile j: ... PV0(j-1) S0(j) PV1(j-1) S1(j) PV0(j)
+// S0(j+1) PV1(j) S1(j+1) ..., so while one warpgroup turns its scores into P,
+// the tensor pipe computes the other tile's P V and next scores.  Q, S, P and
+// O live in TMEM (S0 cols [0,64), S1 [64,128), O0 [128,256), O1 [256,384),
+// Q0 [384,448), Q1 [448,512); P_t over the first 32 columns of S_t, which the
+// in-order tensor pipe reads for P V before the next S MMA overwrites them):
+// the softmax threads copy their Q rows from the TMA tile into TMEM once and
+// write P as FP16 pairs with tcgen05.st, and both MMAs take their A operand
+// straight from TMEM, so the tensor pipe reads only K and V from shared
+// memory.  O accumulates across tiles;
+// a row's running max only moves -- and its O row is rescaled in TMEM -- when
+// a tile's max exceeds it by more than 2^8, so P = exp2(s - max) <= 256 in
+// FP16 and rescales are rare.  V enters the P V MMA as an MN-major operand
+// straight from its TMA tile (keys x 128-byte rows of head dims): no transpose.
+// ---------------------------------------------------------------------------
+namespace pp {
+constexpr int kTileKeys = 64;                      // keys per tile
+constexpr int kStages = 3;                     // K and V ring depth
+constexpr int kQBytes = 128 * 128 * 2;         // query tile: 128 rows x 128 dims
+constexpr int kKVBytes = kTileKeys * 128 * 2;      // K or V tile: 64 keys x 128 dims
+constexpr int kQ = 0;                          // Q0, Q1 (K-major, 2 atoms each)
+constexpr int kK = kQ + 2 * kQBytes;           // K stages (K-major, 2 atoms each)
+constexpr int kV = kK + kStages * kKVBytes;    // V stages (MN-major, 2 boxes each)
+constexpr int kBars = kV + kStages * kKVBytes;
+constexpr int kNumBars = 2 + 4 * kStages + 8 + 1;
+constexpr int kSmem = kBars + kNumBars * 8 + 16 + 1024;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;
+}  // namespace pp
+
+__global__ void __launch_bounds__(pp::kThreads, 1)
+    prefill_attention_pp_kernel(const __grid_constant__ CUtensorMap qmap,
+                                const __grid_constant__ CUtensorMap kmap,
+                                const __grid_constant__ CUtensorMap vmap,
+                                const int32_t* __restrict__ q_start, __half* __restrict__ out,
+                                int q_heads, int kv_heads, int queries, int keys, int bm, int hp,
+                                int q_blocks, float scale_log2, int causal) {
+  using namespace pp;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t sQ = s_base + kQ, sK = s_base + kK, sV = s_base + kV;
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + kBars);
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;  // [2]
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_done = p_full + 2;         // [2]
+  uint64_t* turn = o_done + 2;           // [2] softmax turn of warpgroup t
+  uint64_t* q_tmem = turn + 2;           // both Q tiles copied into TMEM
+  uint64_t* drain = q_tmem + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = q_heads / kv_heads, subgroups = group / hp;
+  const int n_units = q_blocks * subgroups;
+  const int hk = static_cast<int>(blockIdx.y) % kv_heads;
+  const int b = static_cast<int>(blockIdx.y) / kv_heads;
+  const long long qs = q_start != nullptr ? q_start[b] : 0;
+  // Units (query block, head subgroup), last query blocks first; this CTA
+  // takes units u0 (tile 0) and u0 + 1 (tile 1, if it exists).
+  const int u0 = 2 * static_cast<int>(blockIdx.x);
+  const bool has1 = u0 + 1 < n_units;
+  auto unit_m0 = [&](int u) { return (q_blocks - 1 - u / subgroups) * bm; };
+  long long cta_last = keys - 1;  // unit u0 has the later queries
+  if (causal) cta_last = min(cta_last, qs + min(unit_m0(u0) + bm, queries) - 1);
+  const int n_tiles = cta_last >= 0 ? static_cast<int>(cta_last / kTileKeys) + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
+      mbar_init(&turn[t], 128);
+    }
+    mbar_init(q_tmem, 256);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      const int tiles_q = has1 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(tiles_q * hp * 2 * bm * 128));
+      for (int t = 0; t < tiles_q; ++t) {
+        const int u = u0 + t, m0 = unit_m0(u), gs = u % subgroups;
+        for (int g = 0; g < hp; ++g) {
+          const int plane = b * q_heads + hk * group + gs * hp + g;
+          for (int a = 0; a < 2; ++a)
+            tma_load_3d(sQ + t * kQBytes + a * (kQBytes / 2) + g * bm * 128, &qmap, q_full, a * 64,
+                        m0, plane);
+        }
+      }
+      const int plane = b * kv_heads + hk;
+      bool ok = true;
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j % kStages;
+        const uint32_t wait_phase = static_cast<uint32_t>((j / kStages) - 1) & 1u;
+        if (j >= kStages && !wait_or_abort(&k_empty[s], wait_phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[s], kKVBytes);
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(sK + s * kKVBytes + a * (kKVBytes / 2), &kmap, &k_full[s], a * 64, j * kTileKeys,
+                      plane);
+        issued_k = j + 1;
+        if (j >= kStages && !wait_or_abort(&v_empty[s], wait_phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[s], kKVBytes);
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(sV + s * kKVBytes + a * (kKVBytes / 2), &vmap, &v_full[s], a * 64, j * kTileKeys,
+                      plane);
+        issued_v = j + 1;
+      }
+      if (!ok) {  // leave no copy in flight into this CTA's shared memory
+        *abort_flag = 1;
+        mbar_wait(q_full, 0, kDevErrTmaTimeout);
+        for (int j = max(0, issued_k - kStages); j < issued_k; ++j)
+          mbar_wait(&k_full[j % kStages], (j / kStages) & 1, kDevErrTmaTimeout);
+        for (int j = max(0, issued_v - kStages); j < issued_v; ++j)
+          mbar_wait(&v_full[j % kStages], (j / kStages) & 1, kDevErrTmaTimeout);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, kTileKeys);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, 128) | kIdescBMajorMN;
+      // Descriptors of the tile bases; a byte offset moves the start-address
+      // field by offset / 16 (no carry: shared addresses stay below 256 KB).
+      const uint64_t dk = smem_desc_sw128(sK);
+      const uint64_t dv = smem_desc_sw128_mn(sV, kKVBytes / 2, 1024);
+      auto issue_s = [&](int t, int j) {
+        const uint64_t k = dk + ((j % kStages) * kKVBytes >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16_tmem_a(tmem + t * kTileKeys, tmem + 384 + t * 64 + kk * 8,
+                            k + (((kk >> 2) * (kKVBytes / 2) + (kk & 3) * 32) >> 4), idesc_s,
+                            kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint64_t v = dv + ((j % kStages) * kKVBytes >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kTileKeys / 16; ++kk)
+          tc_mma_f16_tmem_a(tmem + 128 + t * 128, tmem + t * kTileKeys + kk * 8,
+                            v + (kk * 2048 >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[t]);
+      };
+      bool ok = spin_or_abort(q_tmem, 0, abort_flag) && spin_or_abort(&k_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        tc_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int sj = j % kStages;
+        for (int t = 0; t < 2; ++t) {
+          ok = spin_or_abort(&p_full[t], j & 1, abort_flag) &&
+               (t == 1 || spin_or_abort(&v_full[sj], (j / kStages) & 1, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == 1) tc_commit(&v_empty[sj]);
+          if (j + 1 < n_tiles) {
+            const int s1 = (j + 1) % kStages;
+            if (t == 0) {
+              ok = spin_or_abort(&k_full[s1], ((j + 1) / kStages) & 1, abort_flag);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_s(t, j + 1);
+            if (t == 1) tc_commit(&k_empty[s1]);
+          }
+        }
+      }
+      if (!ok) {  // no MMA may write TMEM after it is released
+        *abort_flag = 1;
+        tc_commit(drain);
+        mbar_wait(drain, 0, kDevErrMmaTimeout);
+      }
+    }
+  } else {
+    // ---------------- softmax warpgroups ----------------
+    const int tt = warp >> 2, r = threadIdx.x & 127;
+    const bool unit_ok = tt == 0 || has1;
+    const int u = u0 + tt;
+    const int m0 = unit_ok ? unit_m0(u) : 0, gs = u % subgroups;
+    const int g = r / bm, i = r % bm;
+    const bool row_ok = unit_ok && g < hp && m0 + i < queries;
+    long long last = keys - 1;  // last key the row sees (< 0: none)
+    if (causal) last = min(last, qs + m0 + i);
+    if (!row_ok) last = -1;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t t_s = t_lane + tt * kTileKeys, t_o = t_lane + 128 + tt * 128;
+    const uint32_t t_p = t_s;  // P_t over the first 32 columns of S_t
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    if (n_tiles > 0) {
+      // This row of Q_t: from the swizzled TMA tile into TMEM columns
+      // [384 + 64 t, 448 + 64 t), dims 2q and 2q + 1 in column q.
+      ok = __all_sync(0xffffffffu, wait_or_abort(q_full, 0, abort_flag));
+      if (ok) {
+        const uint32_t q_row = sQ + tt * kQBytes + r * 128;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {  // dims 32h .. 32h + 31: chunks 4h .. 4h + 3
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int ch = 4 * h + c;
+            const uint32_t a = q_row + (ch >> 3) * (kQBytes / 2) + (((ch & 7) ^ (r & 7)) << 4);
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                         : "r"(a));
+          }
+          tmem_st16(t_lane + 384 + tt * 64 + 16 * h, w);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(q_tmem);
+      }
+    }
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[tt], j & 1, abort_flag));
+      if (!ok) break;
+      // The two warpgroups take turns: warpgroup 0 runs tile j after warpgroup 1
+      // finished tile j - 1, warpgroup 1 after warpgroup 0 finished tile j, so
+      // each runs alone on the SM's issue slots and exp units while the tensor
+      // pipe works on the other's tile.
+      if (tt == 1 || j > 0) {
+        ok = __all_sync(0xffffffffu, wait_or_abort(&turn[tt], (tt == 1 ? j : j - 1) & 1, abort_flag));
+        if (!ok) break;
+      }
+      tc_fence_after();
+      uint32_t sr[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld16(t_s + c * 16, sr[c]);
+      tmem_ld_wait();
+      const int key0 = j * kTileKeys;
+      if (!__all_sync(0xffffffffu, key0 + kTileKeys - 1 <= last)) {  // mask keys past `last`
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (key0 + c * 16 + e > last) sr[c][e] = 0xff800000u;  // -inf
+      }
+      float part[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        part[e] = fmaxf(fmaxf(__uint_as_float(sr[0][e]), __uint_as_float(sr[0][e + 8])),
+                        fmaxf(__uint_as_float(sr[1][e]), __uint_as_float(sr[1][e + 8])));
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        part[e] = fmaxf(part[e], fmaxf(fmaxf(__uint_as_float(sr[2][e]), __uint_as_float(sr[2][e + 8])),
+                                       fmaxf(__uint_as_float(sr[3][e]), __uint_as_float(sr[3][e + 8]))));
+      const float mx = fmaxf(fmaxf(fmaxf(part[0], part[1]), fmaxf(part[2], part[3])),
+                             fmaxf(fmaxf(part[4], part[5]), fmaxf(part[6], part[7])));
+      const float m_tile = mx * scale_log2;  // scale_log2 > 0
+      const bool grow = m_tile > m_run + kRescaleLog2;
+      float alpha = 1.f;
+      if (grow) {
+        alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_tile);
+        l_run *= alpha;
+        m_run = m_tile;
+      }
+      // P = exp2(s * scale * log2 e - max) as FP16 pairs (two exponentials per
+      // exp-unit op), and this tile's row sum of exactly those FP16 weights.
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;  // no key seen: all s are -inf
+      uint32_t pk[4][8];
+      float psum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const uint32_t x = pack_half2(fmaf(__uint_as_float(sr[c][e]), scale_log2, -m_use),
+                                        fmaf(__uint_as_float(sr[c][e + 1]), scale_log2, -m_use));
+          const uint32_t h = ex2_f16x2(x);
+          pk[c][e >> 1] = h;
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+          psum[(e >> 1) & 3] += f.x + f.y;
+        }
+      // P_t and O_t are free once this warpgroup's previous P V has completed.
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[tt], (j - 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {  // rescale this warp's O rows in TMEM
+#pragma unroll 1
+          for (int c = 0; c < 128; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(t_o + c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st16(t_o + c, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      // Keys 2q, 2q + 1 of the tile go to column q of this row of P_t.
+      const uint32_t lo[16] = {pk[0][0], pk[0][1], pk[0][2], pk[0][3], pk[0][4], pk[0][5],
+                               pk[0][6], pk[0][7], pk[1][0], pk[1][1], pk[1][2], pk[1][3],
+                               pk[1][4], pk[1][5], pk[1][6], pk[1][7]};
+      const uint32_t hi[16] = {pk[2][0], pk[2][1], pk[2][2], pk[2][3], pk[2][4], pk[2][5],
+                               pk[2][6], pk[2][7], pk[3][0], pk[3][1], pk[3][2], pk[3][3],
+                               pk[3][4], pk[3][5], pk[3][6], pk[3][7]};
+      tmem_st16(t_p, lo);
+      tmem_st16(t_p + 16, hi);
+      tmem_st_wait();
+      l_run += (psum[0] + psum[1]) + (psum[2] + psum[3]);
+      tc_fence_before();
+      mbar_arrive(&p_full[tt]);
+      mbar_arrive(&turn[1 - tt]);
+    }
+    if (ok && n_tiles > 0)
+      ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[tt], (n_tiles - 1) & 1, abort_flag));
+    if (!ok) {
+      if (lane == 0) *abort_flag = 1;
+    } else {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint4* orow = reinterpret_cast<uint4*>(
+          out + ((static_cast<size_t>(b) * q_heads + hk * group + gs * hp + g) * queries + m0 + i) *
+                    128);
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 16) {
+        uint32_t o[16];
+        if (n_tiles > 0) {
+          tmem_ld16(t_o + c, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+          float f[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(o[e]) * inv;
+          orow[c / 8] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]),
+                                   pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+          orow[c / 8 + 1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]),
+                                       pack_half2(f[12], f[13]), pack_half2(f[14], f[15]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int launch_pp(const void* q, const void* k, const void* v, const int32_t* q_start, __half* out,
+              int batch, int q_heads, int kv_heads, int queries, int keys, int max_seq, int bm,
+              int hp, int q_blocks, float scale_log2, int causal, cudaStream_t stream) {
+  CUtensorMap qm, km, vm;
+  int rc = make_tensor_map_3d(&qm, q, 128, queries, static_cast<uint64_t>(batch) * q_heads,
+                              static_cast<uint64_t>(queries) * 256, bm, 64);
+  if (rc) return rc;
+  const uint64_t rows = keys > 0 ? keys : 1;
+  rc = make_tensor_map_3d(&km, k, 128, rows, static_cast<uint64_t>(batch) * kv_heads,
+                          static_cast<uint64_t>(max_seq) * 256, pp::kTileKeys, 64);
+  if (rc) return rc;
+  rc = make_tensor_map_3d(&vm, v, 128, rows, static_cast<uint64_t>(batch) * kv_heads,
+                          static_cast<uint64_t>(max_seq) * 256, pp::kTileKeys, 64);
+  if (rc) return rc;
+  auto kern = prefill_attention_pp_kernel;
+  NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pp::kSmem));
+  const int n_units = q_blocks * (q_heads / kv_heads / hp);
+  LaunchCfg cfg;
+  cfg.grid = dim3((n_units + 1) / 2, batch * kv_heads);
+  cfg.block = dim3(pp::kThreads);
+  cfg.smem = pp::kSmem;
+  cfg.stream = stream;
+  return launch(cfg, kern, qm, km, vm, q_start, out, q_heads, kv_heads, queries, keys, bm, hp,
+                q_blocks, scale_log2, causal);
+}
+
 }  // namespace
 
 // Rows of one head per CTA (a power of two, 16..128, covering `queries` when it
@@ -391,6 +811,9 @@ int prefill_attention_run(const void* q, const void* k, const void* v, const int
   const __half* kh = static_cast<const __half*>(k);
   const __half* vh = static_cast<const __half*>(v);
   __half* oh = static_cast<__half*>(out);
+  if (head_dim == 128 && scale > 0.f)
+    return launch_pp(q, k, v, q_start, oh, batch, q_heads, kv_heads, queries, keys, max_seq, bm,
+                     hp, q_blocks, scale_log2, causal ? 1 : 0, stream);
   switch (head_dim) {
     case 32:
       return launch_pa<32>(qh, kh, vh, q_start, oh, batch, q_heads, kv_heads, queries, keys,

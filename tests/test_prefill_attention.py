@@ -105,10 +105,24 @@ def test_small_query_blocks_and_wide_groups(cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("scale", [128 ** -0.5, -0.05])
+def test_head128_paths(cuda, scale):
+    """Head size 128: a positive scale runs the two-tile pipelined kernel, a
+    negative one the single-tile kernel; both against the oracle, including a
+    key count that is not a multiple of the 64-key tile."""
+    q, k, v = _inputs(8, 2, 300, 333, 128, batch=2, capacity=352, seed=31)
+    for causal in (False, True):
+        got = _run(q, k, v, 333, causal, q_start=[33, 0], scale=scale)
+        _check(got, oracle.attention_prefill(q, k, v, 333, scale, causal, q_start=[33, 0]))
+
+
+@pytest.mark.gpu
 def test_no_keys_and_rejections(cuda):
     from llm_compiler_3_b200 import _native
     q, k, v = _inputs(2, 1, 16, 16, 32)
     assert torch.count_nonzero(_run(q, k, v, 0, False)) == 0
+    q, k, v = _inputs(2, 1, 16, 16, 128)
+    assert torch.count_nonzero(_run(q, k, v, 0, True)) == 0
     with pytest.raises(_native.NpuError, match="head_dim"):
         _run(seeded((1, 2, 4, 48), 1), seeded((1, 1, 8, 48), 2), seeded((1, 1, 8, 48), 3), 8, False)
     with pytest.raises(_native.NpuError, match="keys"):
