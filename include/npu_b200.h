@@ -338,6 +338,33 @@ NPU_B200_API int npu_b200_decode_step_device(npu_b200_ctx* ctx, const int32_t* d
                                              const int32_t* d_positions, int batch,
                                              int32_t* d_out_ids, void* stream);
 
+/* Graph plans: a captured module run as a sequence of this library's kernels.
+ *
+ * The B200 counterpart of compiling a capture and running the program on the
+ * reference's simulator (tools/npu-compile/npu-compile.cpp; the run with the
+ * captured arguments, examples/pytorch/mlp.py): `dir` is a capture directory
+ * (arguments.txt, arg<N>.bin, python/npu/capture/export.py:30-40) plus the
+ * graph.txt that llm_compiler_3_b200/graph.py writes from a torch.export of the
+ * module -- FP16 linear layers (+ bias, + ReLU) and scaled-dot-product attention
+ * (causal or not, GQA), the ops of the reference's MLP and SDPA integration
+ * cases (examples/pytorch/mlp.py, test/Integration/attention.py).  Decoder
+ * layers and stacks run through npu_b200_load_plan instead.
+ *
+ * npu_b200_graph_check: parses and checks dir/graph.txt on the host (shapes,
+ *   kernel limits, parameter files); out[0..5] = inputs, outputs, ops, parameter
+ *   bytes, temporary bytes, attention ops that run as flash-decoding.
+ * npu_b200_load_graph: the same checks, then parameters and temporaries into
+ *   device memory owned by the context (one graph per context; loading another
+ *   replaces it).
+ * npu_b200_run_graph: args[i] / outs[i] are device pointers to the i-th input /
+ *   output of graph.txt (in their line order), FP16, contiguous, 16-byte
+ *   aligned; stream-ordered on `stream`.  Calls on one context must not overlap
+ *   on the GPU (they share the temporaries). */
+NPU_B200_API int npu_b200_graph_check(const char* dir, int64_t* out, int n);
+NPU_B200_API int npu_b200_load_graph(npu_b200_ctx* ctx, const char* dir);
+NPU_B200_API int npu_b200_run_graph(npu_b200_ctx* ctx, void* const* args, void* const* outs,
+                                    void* stream);
+
 /* The layers only, on hidden states: x [batch, hidden] FP16 in, y [batch, hidden]
  * FP16 out (the captured decoder layer's function, examples/llama/capture.py:38-54,
  * as a decode step).  Host-buffer version synchronizes `stream`. */

@@ -45,6 +45,14 @@ int make_tensor_map_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64
                        uint64_t planes, uint64_t plane_bytes, uint32_t box_rows,
                        uint32_t box_cols);
 
+// Graph plans (graph.cu): the state a context holds once npu_b200_load_graph
+// succeeded, freed by graph_free; runtime.cu owns the context and exposes its
+// device and graph slot.
+struct GraphState;
+void graph_free(GraphState* g);
+int ctx_device(const npu_b200_ctx* c);
+GraphState*& ctx_graph(npu_b200_ctx* c);
+
 // Launch helper: enables programmatic dependent launch when `pdl` is set.
 struct LaunchCfg {
   dim3 grid, block;

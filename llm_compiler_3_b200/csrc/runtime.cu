@@ -304,6 +304,7 @@ struct npu_b200_ctx {
   std::vector<void*> px_opened;  // peers' IPC mappings, closed before the local buffers are freed
   bool px_ready = false;         // false: the all-reduces go through NCCL
   PeerExchange px;               // seq filled in per exchange
+  GraphState* graph = nullptr;   // npu_b200_load_graph (graph.cu)
 };
 
 namespace npu_b200 {
@@ -948,6 +949,11 @@ int check_positions(const npu_b200_ctx* c, const int32_t* h_positions, int batch
 }  // namespace
 }  // namespace npu_b200
 
+namespace npu_b200 {
+int ctx_device(const npu_b200_ctx* c) { return c->device; }
+GraphState*& ctx_graph(npu_b200_ctx* c) { return c->graph; }
+}  // namespace npu_b200
+
 // ===========================================================================
 // C ABI
 // ===========================================================================
@@ -1360,6 +1366,8 @@ extern "C" int npu_b200_destroy(npu_b200_ctx* c) {
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
   release(c);
+  graph_free(c->graph);
+  c->graph = nullptr;
   if (c->comm && g_nccl.CommDestroy) g_nccl.CommDestroy(c->comm);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;

@@ -160,3 +160,62 @@ class Decoder:
             self.close()
         except Exception:
             pass
+
+
+class GraphRunner:
+    """A graph plan (``graph.capture_graph``) loaded into its own libnpu_b200
+    context: the B200 counterpart of compiling a capture and running the
+    program with the captured arguments (examples/pytorch/mlp.py)."""
+
+    def __init__(self, directory: str | Path, device: int = 0):
+        from .graph import GraphPlan
+        self.lib = _native.lib()
+        self.device = device
+        self.directory = Path(directory)
+        self.plan = GraphPlan.parse((self.directory / "graph.txt").read_text())
+        self._ctx = ctypes.c_void_p()
+        _native.check(self.lib.npu_b200_create(device, 0, 1, None, ctypes.byref(self._ctx)))
+        try:
+            _native.check(self.lib.npu_b200_load_graph(self._ctx, str(self.directory).encode()))
+        except Exception:
+            self.close()
+            raise
+
+    def run(self, *inputs: torch.Tensor, outs: Iterable[torch.Tensor] | None = None
+            ) -> list[torch.Tensor]:
+        """Run the graph on CUDA FP16 inputs (graph.txt order) on the current
+        stream; returns the outputs (allocated unless `outs` is given)."""
+        dev = torch.device("cuda", self.device)
+        if len(inputs) != len(self.plan.inputs):
+            raise ValueError(f"graph takes {len(self.plan.inputs)} inputs, got {len(inputs)}")
+        for name, t in zip(self.plan.inputs, inputs):
+            want = self.plan.tensors[name][1]
+            if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous() or \
+                    t.numel() != int(np.prod(want)):
+                raise ValueError(f"input {name}: need a contiguous CUDA float16 tensor of {want}")
+        if outs is None:
+            outs = [torch.empty(self.plan.tensors[n][1], dtype=torch.float16, device=dev)
+                    for n in self.plan.outputs]
+        outs = list(outs)
+        args = (ctypes.c_void_p * max(1, len(inputs)))(*[t.data_ptr() for t in inputs])
+        res = (ctypes.c_void_p * max(1, len(outs)))(*[t.data_ptr() for t in outs])
+        _native.check(self.lib.npu_b200_run_graph(
+            self._ctx, args, res, ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+        return outs
+
+    def close(self) -> None:
+        if self._ctx:
+            _native.check(self.lib.npu_b200_destroy(self._ctx))
+            self._ctx = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass

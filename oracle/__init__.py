@@ -15,3 +15,4 @@ follows; ``tests/golden/`` pins it against ``transformers`` itself and against
 the reference's own known-answer tests.
 """
 from .decode import *  # noqa: F401,F403
+from .graph import run_graph_plan  # noqa: F401
