@@ -24,7 +24,10 @@ decode plan (``plan.py``, ``runtime.Decoder``) instead.
 
 The capture directory keeps the reference's format (``arguments.txt`` plus
 little-endian ``arg<N>.bin``, activations first, then parameters and buffers
-sorted by name, export.py:30-40, 117-119, 133-138) and adds ``graph.txt``:
+sorted by name, export.py:30-40, 117-119, 133-138) and adds ``metadata.json``
+(the package's ABI description, as npu-compile writes one beside its program,
+tools/npu-compile/npu-compile.cpp:479-507, lib/Transforms/Emit.cpp:1424-1430)
+and ``graph.txt``:
 
     npu.stage cuda-graph
     npu.schema 1
@@ -38,6 +41,7 @@ pointers, each in the order of their lines.
 """
 from __future__ import annotations
 
+import json
 import math
 import operator
 from dataclasses import dataclass, field
@@ -264,4 +268,22 @@ def capture_graph(module: torch.nn.Module, example: Sequence[torch.Tensor],
     plan.tensors = ordered
     path = directory / "graph.txt"
     path.write_text(plan.text())
+    arguments = [{"index": i, "name": f"input{i}", "role": "input", "shape": list(t.shape),
+                  "dtype": _dtype_name(t), "bytes": t.numel() * t.element_size()}
+                 for i, t in enumerate(example)]
+    for name, (role, dims, arg) in plan.tensors.items():
+        if role == "param":
+            arguments.append({"index": arg, "name": name, "role": "param", "shape": list(dims),
+                              "dtype": "float16", "bytes": 2 * math.prod(dims)})
+    arguments.sort(key=lambda a: a["index"])
+    metadata = {
+        "schema": "npu.b200.graph.v1", "stage": STAGE, "numerical_policy": "fp16",
+        "arguments": arguments,
+        "outputs": [{"name": n, "shape": list(plan.tensors[n][1]), "dtype": "float16"}
+                    for n in plan.outputs],
+        "ops": [op[0] for op in plan.ops],
+        "param_bytes": sum(a["bytes"] for a in arguments if a["role"] == "param"),
+        "temp_bytes": sum(2 * math.prod(d) for r, d, _ in plan.tensors.values() if r == "temp"),
+    }
+    (directory / "metadata.json").write_text(json.dumps(metadata, indent=2) + "\n")
     return path

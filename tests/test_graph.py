@@ -9,6 +9,7 @@ On the CPU: the plan the emitter writes, the host-side checks of the C ABI, and
 the oracle's interpretation of the plan against the module itself.  On the GPU:
 the library running the plan against the oracle (max-abs 2e-2, cosine 0.9999)."""
 import ctypes
+import json
 
 import pytest
 import torch
@@ -96,6 +97,11 @@ def test_mlp_plan(tmp_path, hidden, inner, rows):
     assert [a.split()[1] for a in args[1:5]] == ["down.bias", "down.weight", "up.bias", "up.weight"]
     params = 2 * (2 * hidden * inner + hidden + inner)
     assert _check_info(tmp_path) == [1, 1, 2, params, 2 * rows * inner, 0]
+    meta = json.loads((tmp_path / "metadata.json").read_text())
+    assert meta["schema"] == "npu.b200.graph.v1" and meta["numerical_policy"] == "fp16"
+    assert [a["index"] for a in meta["arguments"]] == list(range(5))
+    assert meta["param_bytes"] == params and meta["outputs"][0]["shape"] == [rows, hidden]
+    assert meta["ops"] == ["linear", "linear"]
     got = oracle.run_graph_plan(tmp_path, [x])[0]
     with torch.no_grad():
         want = model.float()(x.float())
