@@ -12,6 +12,12 @@ torch-mlir -- for graphs built from the ops the library has kernels for:
   reference's normalizeGraph fuses maximumf into the matmul epilogue,
   lib/Transforms/Normalize.cpp:494-507): the tcgen05 linear kernel, 128 rows per
   launch;
+* ``aten.matmul`` / ``aten.mm`` / ``aten.addmm`` by a 2-D parameter W [K, N]
+  that nothing else reads: the same linear kernel, with W stored transposed
+  ([N, K]) in its arg<N>.bin and listed under ``pretransposed`` in metadata.json
+  -- the flip the reference's normalizeGraph records for its image builder
+  (pretransposeWeights, lib/Transforms/Normalize.cpp:670-701), in the other
+  direction, once at capture time;
 * ``aten.scaled_dot_product_attention`` (no mask, no dropout, causal or not, GQA,
   any scale) -- npu.attention after canonicalizeAttention
   (lib/Transforms/Attention.cpp:384-419): the flash-decoding kernel for one
@@ -70,6 +76,7 @@ class GraphPlan:
     ops: list[tuple] = field(default_factory=list)
     inputs: list[str] = field(default_factory=list)
     outputs: list[str] = field(default_factory=list)
+    pretransposed: set[str] = field(default_factory=set)  # parameters stored as W^T
 
     def text(self) -> str:
         lines = [f"npu.stage {STAGE}", f"npu.schema {SCHEMA}"]
@@ -143,6 +150,28 @@ def build_graph_plan(exported) -> tuple[GraphPlan, list[str], dict[str, torch.Te
     nodes = list(graph.nodes)
     name_of: dict[str, str] = {}  # fx node -> plan tensor (through aliases)
     fused_relu: set[str] = set()
+    pretransposed: set[str] = set()
+
+    def emit_linear(node, x, w, b, weight_kn: bool):
+        users = list(node.users)
+        relu = len(users) == 1 and str(users[0].target) == "aten.relu.default"
+        if relu:
+            fused_relu.add(users[0].name)
+        wn = name_of[w.name]
+        if plan.tensors.get(wn, ("",))[0] != "param" or len(_shape(w)) != 2:
+            raise GraphUnsupported(f"{node.name}: the weight must be a 2-D parameter")
+        if weight_kn:  # x @ W with W [K, N]: store W^T, the linear kernel's [N, K]
+            if len(w.users) != 1 or wn in pretransposed:
+                raise GraphUnsupported(f"{node.name}: a matmul weight must have no other reader")
+            k, n = _shape(w)
+            params[wn] = params[wn].t().contiguous()
+            plan.tensors[wn] = ("param", (n, k), None)
+            pretransposed.add(wn)
+        out = users[0] if relu else node
+        plan.tensors[node.name] = ("temp", _shape(out), None)
+        name_of[node.name] = node.name
+        plan.ops.append(("linear", node.name, name_of[x.name], wn,
+                         name_of[b.name] if b is not None else None, relu))
 
     for node in nodes:
         if node.op == "placeholder":
@@ -171,21 +200,17 @@ def build_graph_plan(exported) -> tuple[GraphPlan, list[str], dict[str, torch.Te
                                            "with it as the only user")
                 name_of[node.name] = name_of[src.name]
             elif target == "aten.linear.default":
-                x, w = node.args[0], node.args[1]
                 b = node.args[2] if len(node.args) > 2 else None
-                users = list(node.users)
-                relu = len(users) == 1 and str(users[0].target) == "aten.relu.default"
-                if relu:
-                    fused_relu.add(users[0].name)
-                wn = name_of[w.name]
-                if plan.tensors.get(wn, ("",))[0] != "param":
-                    raise GraphUnsupported(f"{node.name}: the weight must be a parameter")
-                out = (users[0] if relu else node)
-                dims = _shape(out)
-                plan.tensors[node.name] = ("temp", dims, None)
-                name_of[node.name] = node.name
-                plan.ops.append(("linear", node.name, name_of[x.name], wn,
-                                 name_of[b.name] if b is not None else None, relu))
+                emit_linear(node, node.args[0], node.args[1], b, weight_kn=False)
+            elif target in ("aten.matmul.default", "aten.mm.default"):
+                emit_linear(node, node.args[0], node.args[1], None, weight_kn=True)
+            elif target == "aten.addmm.default":
+                beta = node.kwargs.get("beta", 1)
+                alpha = node.kwargs.get("alpha", 1)
+                bias = node.args[0]
+                if beta != 1 or alpha != 1 or len(_shape(bias)) != 1:
+                    raise GraphUnsupported(f"{node.name}: addmm needs a [N] bias, beta = alpha = 1")
+                emit_linear(node, node.args[1], node.args[2], bias, weight_kn=True)
             elif target == "aten.scaled_dot_product_attention.default":
                 a = list(node.args) + [None] * 6
                 q, k, v = a[0], a[1], a[2]
@@ -233,6 +258,7 @@ def build_graph_plan(exported) -> tuple[GraphPlan, list[str], dict[str, torch.Te
     used |= {o[4] for o in plan.ops if o[0] == "linear" and o[4]}
     used |= {n for o in plan.ops if o[0] == "sdpa" for n in o[2:5]}
     plan.aliases = {k: v for k, v in plan.aliases.items() if k in used}
+    plan.pretransposed = pretransposed
     return plan, user_inputs, params
 
 
@@ -282,6 +308,7 @@ def capture_graph(module: torch.nn.Module, example: Sequence[torch.Tensor],
         "outputs": [{"name": n, "shape": list(plan.tensors[n][1]), "dtype": "float16"}
                     for n in plan.outputs],
         "ops": [op[0] for op in plan.ops],
+        "pretransposed": sorted(plan.tensors[n][2] for n in plan.pretransposed),
         "param_bytes": sum(a["bytes"] for a in arguments if a["role"] == "param"),
         "temp_bytes": sum(2 * math.prod(d) for r, d, _ in plan.tensors.values() if r == "temp"),
     }

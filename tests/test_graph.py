@@ -140,6 +140,36 @@ def test_views_and_scale(tmp_path):
     assert GraphPlan.parse(path.read_text()).ops[0][5] == pytest.approx(0.05)
 
 
+class MatmulParams(torch.nn.Module):
+    """x @ W with W [K, N] parameters, one through addmm with a bias."""
+
+    def __init__(self):
+        super().__init__()
+        g = torch.Generator().manual_seed(9)
+        self.w1 = torch.nn.Parameter(torch.randn(64, 128, generator=g) / 8)
+        self.w2 = torch.nn.Parameter(torch.randn(128, 64, generator=g) / 11)
+        self.b = torch.nn.Parameter(torch.randn(64, generator=g) / 10)
+
+    def forward(self, x):
+        return torch.addmm(self.b, torch.relu(x @ self.w1), self.w2)
+
+
+def test_matmul_weights_are_pretransposed(tmp_path):
+    from llm_compiler_3_b200.graph import GraphPlan, capture_graph
+    model = MatmulParams().half()
+    x = seeded((32, 64), 6, 0.5)
+    path = capture_graph(model, (x,), tmp_path)
+    plan = GraphPlan.parse(path.read_text())
+    assert [(op[0], op[5]) for op in plan.ops] == [("linear", True), ("linear", False)]
+    assert plan.tensors["w1"][1] == (128, 64) and plan.tensors["w2"][1] == (64, 128)
+    meta = json.loads((tmp_path / "metadata.json").read_text())
+    assert meta["pretransposed"] == sorted([plan.tensors["w1"][2], plan.tensors["w2"][2]])
+    got = oracle.run_graph_plan(tmp_path, [x])[0]
+    with torch.no_grad():
+        want = model.float()(x.float())
+    assert float((got - want).abs().max()) <= 0.01 * float(want.abs().max())
+
+
 def test_unsupported_modules_are_rejected(tmp_path):
     from llm_compiler_3_b200.graph import GraphUnsupported, capture_graph
 
@@ -163,8 +193,15 @@ def test_unsupported_modules_are_rejected(tmp_path):
     q, k, v = _sdpa_inputs(2, 2, 4, 8, 64)
     with pytest.raises(GraphUnsupported, match="mask"):
         capture_graph(Masked(), (q, k, v, torch.zeros(4, 8, dtype=torch.float16)), tmp_path / "a")
-    with pytest.raises(GraphUnsupported, match="no kernel"):
+    with pytest.raises(GraphUnsupported, match="2-D parameter"):
         capture_graph(Matmul(), (seeded((4, 64), 1), seeded((64, 8), 2)), tmp_path / "b")
+
+    class Softmax(torch.nn.Module):
+        def forward(self, x):
+            return torch.softmax(x, dim=-1)
+
+    with pytest.raises(GraphUnsupported, match="no kernel"):
+        capture_graph(Softmax(), (seeded((4, 64), 1),), tmp_path / "d")
     with pytest.raises(GraphUnsupported):
         capture_graph(LoneRelu().half(), (seeded((4, 64), 1),), tmp_path / "c")
 
@@ -240,5 +277,14 @@ def test_views_run(cuda, tmp_path):
     torch.manual_seed(5)
     x = seeded((2, 7, 128), 4, 0.5)
     capture_graph(Flattened().to(torch.float16).eval(), (x,), tmp_path)
+    got = _run_twice(tmp_path, [x])[0]
+    _close(got, oracle.run_graph_plan(tmp_path, [x])[0])
+
+
+@pytest.mark.gpu
+def test_matmul_params_run(cuda, tmp_path):
+    from llm_compiler_3_b200.graph import capture_graph
+    x = seeded((32, 64), 6, 0.5)
+    capture_graph(MatmulParams().half(), (x,), tmp_path)
     got = _run_twice(tmp_path, [x])[0]
     _close(got, oracle.run_graph_plan(tmp_path, [x])[0])
