@@ -295,6 +295,17 @@ NPU_B200_API int npu_b200_load_plan(npu_b200_ctx* ctx, const char* plan_path);
  * npu_b200_load_plan makes); out[] as npu_b200_plan_info with tp_size 1. */
 NPU_B200_API int npu_b200_plan_check(const char* plan_path, int64_t* out, int n);
 
+/* The share of tensor-parallel rank tp_rank of tp_size under the plan, as the
+ * runtime shards the weights when they are set (no counterpart in the
+ * reference, which runs one core array): out[0..4] = q heads, KV heads, FFN
+ * columns, vocabulary rows and the first vocabulary row of this rank.  Rank r
+ * holds q heads [r*out[0], (r+1)*out[0]) and KV heads [r*out[1], (r+1)*out[1])
+ * (rows of q/k/v_proj, columns of o_proj), FFN columns [r*out[2], (r+1)*out[2])
+ * (rows of gate/up_proj, columns of down_proj) and LM-head rows
+ * [out[4], out[4] + out[3]).  Host only: no GPU is needed. */
+NPU_B200_API int npu_b200_shard_info(const char* plan_path, int tp_rank, int tp_size, int64_t* out,
+                                     int n);
+
 /* out[0..11] = layers, hidden, local q heads, local kv heads, local ffn, local vocab,
  * vocab offset, max_batch, max_seq, head_dim, plan fingerprint (FNV-1a), tp_size;
  * out[12] (when n >= 13) = 1 if the tensor-parallel all-reduces run over NVLink

@@ -69,6 +69,7 @@ _SIGNATURES = [
     ("npu_b200_create", c_int, [c_int, c_int, c_int, c_void_p, POINTER(c_void_p)]),
     ("npu_b200_destroy", c_int, [c_void_p]),
     ("npu_b200_graph_check", c_int, [c_char_p, POINTER(c_int64), c_int]),
+    ("npu_b200_shard_info", c_int, [c_char_p, c_int, c_int, POINTER(c_int64), c_int]),
     ("npu_b200_load_graph", c_int, [c_void_p, c_char_p]),
     ("npu_b200_run_graph", c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), c_void_p]),
     ("npu_b200_load_plan", c_int, [c_void_p, c_char_p]),

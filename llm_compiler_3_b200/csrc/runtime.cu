@@ -424,20 +424,42 @@ int setup_peer_exchange(npu_b200_ctx* c) {
   return NPU_B200_OK;
 }
 
+// What tensor-parallel rank r of T holds (Megatron-style): q heads
+// [r q_loc, (r+1) q_loc) and KV heads [r kv_loc, (r+1) kv_loc) of the q/k/v
+// rows and of o_proj's columns, FFN columns [r ffn_loc, (r+1) ffn_loc) of
+// gate/up rows and down_proj columns, vocabulary rows [vocab_off, vocab_off +
+// vocab_loc) of the LM head.
+struct Shard {
+  int q_loc = 0, kv_loc = 0, ffn_loc = 0, vocab_loc = 0, vocab_off = 0;
+};
+
+int shard_layout(const Plan& P, int T, int r, Shard* s) {
+  NPU_REQUIRE(T >= 1 && r >= 0 && r < T, "bad tp rank %d / size %d", r, T);
+  NPU_REQUIRE(P.kv_heads % T == 0, "plan: kv_heads %d not divisible by tp_size %d", P.kv_heads, T);
+  NPU_REQUIRE(P.ffn % (64 * T) == 0, "plan: ffn %d not divisible by 64 * tp_size", P.ffn);
+  s->kv_loc = P.kv_heads / T;
+  s->q_loc = P.heads / T;
+  s->ffn_loc = P.ffn / T;
+  s->vocab_loc = s->vocab_off = 0;
+  if (P.vocab > 0) {
+    s->vocab_loc = (P.vocab + T - 1) / T;
+    s->vocab_off = r * s->vocab_loc;
+    if (s->vocab_off + s->vocab_loc > P.vocab) s->vocab_loc = P.vocab - s->vocab_off;
+    NPU_REQUIRE(s->vocab_loc >= 1, "plan: vocab %d too small for tp_size %d", P.vocab, T);
+  }
+  return NPU_B200_OK;
+}
+
 int allocate(npu_b200_ctx* c) {
   const Plan& P = c->plan;
   const int T = c->tp_size, r = c->tp_rank;
-  NPU_REQUIRE(P.kv_heads % T == 0, "plan: kv_heads %d not divisible by tp_size %d", P.kv_heads, T);
-  NPU_REQUIRE(P.ffn % (64 * T) == 0, "plan: ffn %d not divisible by 64 * tp_size", P.ffn);
-  c->kv_loc = P.kv_heads / T;
-  c->q_loc = P.heads / T;
-  c->ffn_loc = P.ffn / T;
-  if (P.vocab > 0) {
-    c->vocab_loc = (P.vocab + T - 1) / T;
-    c->vocab_off = r * c->vocab_loc;
-    if (c->vocab_off + c->vocab_loc > P.vocab) c->vocab_loc = P.vocab - c->vocab_off;
-    NPU_REQUIRE(c->vocab_loc >= 1, "plan: vocab %d too small for tp_size %d", P.vocab, T);
-  }
+  Shard sh;
+  if (int rc0 = shard_layout(P, T, r, &sh)) return rc0;
+  c->kv_loc = sh.kv_loc;
+  c->q_loc = sh.q_loc;
+  c->ffn_loc = sh.ffn_loc;
+  c->vocab_loc = sh.vocab_loc;
+  c->vocab_off = sh.vocab_off;
   const size_t H = P.hidden, B = P.max_batch, D = P.head_dim;
   int rc = 0;
   c->layers.assign(P.layers, LayerBuffers());
@@ -1037,6 +1059,24 @@ extern "C" int npu_b200_plan_check(const char* plan_path, int64_t* out, int n) {
                          p.max_seq, p.head_dim,
                          static_cast<int64_t>(p.fingerprint & 0x7fffffffffffffffll), 1};
   for (int i = 0; i < 12; ++i) out[i] = v[i];
+  return NPU_B200_OK;
+}
+
+extern "C" int npu_b200_shard_info(const char* plan_path, int tp_rank, int tp_size, int64_t* out,
+                                   int n) {
+  clear_error();
+  NPU_REQUIRE(plan_path && out && n >= 5, "shard_info needs a path and 5 slots");
+  std::ifstream f(plan_path);
+  if (!f) return set_error(NPU_B200_E_PLAN, "cannot read plan %s", plan_path);
+  std::stringstream ss;
+  ss << f.rdbuf();
+  Plan p;
+  int rc = parse_plan(ss.str(), &p);
+  if (rc) return rc;
+  Shard sh;
+  if ((rc = shard_layout(p, tp_size, tp_rank, &sh))) return rc;
+  const int64_t v[5] = {sh.q_loc, sh.kv_loc, sh.ffn_loc, sh.vocab_loc, sh.vocab_off};
+  for (int i = 0; i < 5; ++i) out[i] = v[i];
   return NPU_B200_OK;
 }
 
