@@ -32,3 +32,23 @@ def test_reference_arm_json_line():
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s",
                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched the way the driver launches N > 1 (torchrun, 2 ranks on 127.0.0.1):
+    rank 0 alone runs the sample and prints the one JSON line, every rank exits 0."""
+    import socket
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    done = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                           "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                           "--master-port", str(port), str(ROOT / "bench.py"), "--impl",
+                           "reference", "--gpus", "2", "--steps", "1", "--warmup", "3",
+                           "--batch", "1", "--layers", "1", "--seq", "64"],
+                          capture_output=True, text=True, cwd=ROOT, timeout=900)
+    assert done.returncode == 0, done.stderr[-2000:]
+    lines = [ln for ln in done.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
