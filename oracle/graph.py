@@ -36,7 +36,10 @@ def run_graph_plan(directory: str | Path, inputs: Sequence[torch.Tensor]) -> lis
             continue
         if f[0] == "tensor":
             tensors[f[1]] = (f[2], _dims(f[4]), int(f[6]) if len(f) > 6 else None)
-            (ins if f[2] == "input" else outs if f[2] == "output" else []).append(f[1])
+            if f[2] == "input":
+                ins.append(f[1])
+            elif f[2] == "output":
+                outs.append(f[1])
         elif f[0] == "alias":
             aliases[f[1]] = (f[2], _dims(f[3]))
         elif f[0] == "op":
