@@ -170,6 +170,36 @@ def test_matmul_weights_are_pretransposed(tmp_path):
     assert float((got - want).abs().max()) <= 0.01 * float(want.abs().max())
 
 
+class TwoHeads(torch.nn.Module):
+    """Two outputs, returned in the opposite order of their computation."""
+
+    def __init__(self):
+        super().__init__()
+        self.a = torch.nn.Linear(64, 32)
+        self.b = torch.nn.Linear(64, 48)
+
+    def forward(self, x):
+        first = self.a(x)
+        second = torch.relu(self.b(x))
+        return second, first
+
+
+def test_outputs_bind_in_return_order(tmp_path):
+    from llm_compiler_3_b200.graph import GraphPlan, capture_graph
+    torch.manual_seed(8)
+    model = TwoHeads().half().eval()
+    x = seeded((16, 64), 7, 0.5)
+    path = capture_graph(model, (x,), tmp_path)
+    plan = GraphPlan.parse(path.read_text())
+    assert [plan.tensors[n][1] for n in plan.outputs] == [(16, 48), (16, 32)]
+    assert _check_info(tmp_path)[:3] == [1, 2, 2]
+    got = oracle.run_graph_plan(tmp_path, [x])
+    with torch.no_grad():
+        want = model.float()(x.float())
+    for g, w in zip(got, want):
+        assert float((g - w).abs().max()) <= 0.01 * float(w.abs().max())
+
+
 def test_unsupported_modules_are_rejected(tmp_path):
     from llm_compiler_3_b200.graph import GraphUnsupported, capture_graph
 
