@@ -252,6 +252,18 @@ def test_bad_plans_fail_on_the_host(tmp_path):
     check(text.replace("op linear linear x", "op linear linear linear_1"), "read before")
     check(text.replace("up.bias 1\n", "up.bias 7\n"), "relu 0\\|1")
     check(text.replace("npu.schema 1", "npu.schema 2"), "schema")
+    check(text + "alias xv x 9x64\n", "tensors must precede the ops")
+    lines = text.splitlines(keepends=True)
+    ops_at = next(i for i, ln in enumerate(lines) if ln.startswith("op "))
+    check("".join(lines[:ops_at]) + "alias xv x 9x64\n" + "".join(lines[ops_at:]),
+          "element count")
+    check("".join(lines[:ops_at]) + "tensor spare output f16 4x4\n" + "".join(lines[ops_at:]),
+          "never written")
+    check(text.replace("tensor linear temp f16 8x128", "tensor linear temp f16 8x64"),
+          "not \\[rows, N\\]")
+    (tmp_path / "graph.txt").unlink()
+    with pytest.raises(_native.NpuError, match="cannot read"):
+        _check_info(tmp_path)
     (tmp_path / "graph.txt").write_text(text)
     (tmp_path / "arg4.bin").write_bytes(b"\0" * 10)
     with pytest.raises(_native.NpuError, match="arg4.bin"):
