@@ -106,11 +106,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int group = q_heads / kv_heads;
   const int subgroups = group / hp;
-  // Last query blocks first: under the causal mask they see the most keys.
-  const int qb = q_blocks - 1 - static_cast<int>(blockIdx.x) / subgroups;
-  const int gs = static_cast<int>(blockIdx.x) % subgroups;
-  const int hk = static_cast<int>(blockIdx.y) % kv_heads;
-  const int b = static_cast<int>(blockIdx.y) / kv_heads;
+  // Last query blocks first: under the causal mask they see the most keys.  The
+  // block index is the grid's slow dimension (y), so CTAs are dispatched
+  // heaviest first across every head and sequence.
+  const int qb = q_blocks - 1 - static_cast<int>(blockIdx.y) / subgroups;
+  const int gs = static_cast<int>(blockIdx.y) % subgroups;
+  const int hk = static_cast<int>(blockIdx.x) % kv_heads;
+  const int b = static_cast<int>(blockIdx.x) / kv_heads;
   const int m0 = qb * bm;
   const long long qs = q_start != nullptr ? q_start[b] : 0;
   const size_t kv_base = (static_cast<size_t>(b) * kv_heads + hk) * max_seq;
@@ -342,7 +344,7 @@ int launch_pa(const __half* q, const __half* k, const __half* v, const int32_t* 
   auto kern = prefill_attention_kernel<D>;
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem));
   LaunchCfg cfg;
-  cfg.grid = dim3(q_blocks * (q_heads / kv_heads / hp), batch * kv_heads);
+  cfg.grid = dim3(batch * kv_heads, q_blocks * (q_heads / kv_heads / hp));
   cfg.block = dim3(kThreads);
   cfg.smem = S::kSmem;
   cfg.stream = stream;
@@ -420,12 +422,12 @@ __global__ void __launch_bounds__(pp::kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = q_heads / kv_heads, subgroups = group / hp;
   const int n_units = q_blocks * subgroups;
-  const int hk = static_cast<int>(blockIdx.y) % kv_heads;
-  const int b = static_cast<int>(blockIdx.y) / kv_heads;
+  const int hk = static_cast<int>(blockIdx.x) % kv_heads;
+  const int b = static_cast<int>(blockIdx.x) / kv_heads;
   const long long qs = q_start != nullptr ? q_start[b] : 0;
   // Units (query block, head subgroup), last query blocks first; this CTA
   // takes units u0 (tile 0) and u0 + 1 (tile 1, if it exists).
-  const int u0 = 2 * static_cast<int>(blockIdx.x);
+  const int u0 = 2 * static_cast<int>(blockIdx.y);  // slow grid dimension: heaviest first
   const bool has1 = u0 + 1 < n_units;
   auto unit_m0 = [&](int u) { return (q_blocks - 1 - u / subgroups) * bm; };
   long long cta_last = keys - 1;  // unit u0 has the later queries
@@ -762,7 +764,7 @@ int launch_pp(const void* q, const void* k, const void* v, const int32_t* q_star
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pp::kSmem));
   const int n_units = q_blocks * (q_heads / kv_heads / hp);
   LaunchCfg cfg;
-  cfg.grid = dim3((n_units + 1) / 2, batch * kv_heads);
+  cfg.grid = dim3(batch * kv_heads, (n_units + 1) / 2);
   cfg.block = dim3(pp::kThreads);
   cfg.smem = pp::kSmem;
   cfg.stream = stream;
@@ -804,8 +806,8 @@ int prefill_attention_run(const void* q, const void* k, const void* v, const int
   int bm = 0, hp = 0;
   prefill_blocking(queries, q_heads / kv_heads, &bm, &hp);
   const int q_blocks = (queries + bm - 1) / bm;
-  NPU_REQUIRE(static_cast<long long>(q_blocks) * (q_heads / kv_heads / hp) < (1ll << 31),
-              "prefill_attention: too many query blocks");
+  NPU_REQUIRE(static_cast<long long>(q_blocks) * (q_heads / kv_heads / hp) <= 65535,
+              "prefill_attention: %d queries make too many query blocks", queries);
   const float scale_log2 = scale * 1.4426950408889634f;
   const __half* qh = static_cast<const __half*>(q);
   const __half* kh = static_cast<const __half*>(k);
