@@ -23,7 +23,8 @@ torch-mlir -- for graphs built from the ops the library has kernels for:
   (lib/Transforms/Attention.cpp:384-419): the flash-decoding kernel for one
   query per head without a causal mask, the prefill attention kernel otherwise;
 * views and copies that keep the row-major layout (``view``, ``reshape``,
-  ``contiguous``, ``clone``): aliases, no kernel.
+  ``flatten``, ``squeeze``, ``unsqueeze``, ``contiguous``, ``clone``) and
+  dropout in eval mode: aliases, no kernel.
 
 Decoder layers and stacks (RMSNorm, RoPE, SwiGLU, KV cache) run through the
 decode plan (``plan.py``, ``runtime.Decoder``) instead.
@@ -60,7 +61,9 @@ STAGE = "cuda-graph"
 SCHEMA = 1
 
 _VIEWS = {"aten.view.default", "aten.reshape.default", "aten.contiguous.default",
-          "aten.clone.default", "aten._unsafe_view.default", "aten.alias.default"}
+          "aten.clone.default", "aten._unsafe_view.default", "aten.alias.default",
+          "aten.flatten.using_ints", "aten.unsqueeze.default", "aten.squeeze.dim",
+          "aten.squeeze.dims", "aten.squeeze.default"}
 
 
 class GraphUnsupported(ValueError):
@@ -191,6 +194,14 @@ def build_graph_plan(exported) -> tuple[GraphPlan, list[str], dict[str, torch.Te
             if target in _VIEWS:
                 src = name_of[node.args[0].name]
                 src = plan.aliases[src][0] if src in plan.aliases else src  # base tensor
+                plan.aliases[node.name] = (src, _shape(node))
+                name_of[node.name] = node.name
+            elif target == "aten.dropout.default":
+                train = node.args[2] if len(node.args) > 2 else node.kwargs.get("train", False)
+                if train:
+                    raise GraphUnsupported(f"{node.name}: dropout in training mode")
+                src = name_of[node.args[0].name]
+                src = plan.aliases[src][0] if src in plan.aliases else src
                 plan.aliases[node.name] = (src, _shape(node))
                 name_of[node.name] = node.name
             elif target == "aten.relu.default":

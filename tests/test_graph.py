@@ -184,6 +184,33 @@ class TwoHeads(torch.nn.Module):
         return second, first
 
 
+class Reshaped(torch.nn.Module):
+    """flatten / unsqueeze / squeeze around a linear layer, and eval-mode dropout."""
+
+    def __init__(self):
+        super().__init__()
+        self.lin = torch.nn.Linear(64, 64)
+        self.drop = torch.nn.Dropout(0.1)
+
+    def forward(self, x):
+        y = torch.flatten(x, 0, 1).unsqueeze(0).squeeze(0)
+        return self.drop(self.lin(y)).unsqueeze(1).squeeze(1)
+
+
+def test_layout_preserving_ops_are_aliases(tmp_path):
+    from llm_compiler_3_b200.graph import GraphPlan, capture_graph
+    torch.manual_seed(11)
+    model = Reshaped().half().eval()
+    x = seeded((2, 8, 64), 12, 0.5)
+    path = capture_graph(model, (x,), tmp_path)
+    plan = GraphPlan.parse(path.read_text())
+    assert [op[0] for op in plan.ops] == ["linear"]
+    got = oracle.run_graph_plan(tmp_path, [x])[0]
+    with torch.no_grad():
+        want = model.float()(x.float())
+    assert float((got.reshape(want.shape) - want).abs().max()) <= 0.01 * float(want.abs().max())
+
+
 def test_outputs_bind_in_return_order(tmp_path):
     from llm_compiler_3_b200.graph import GraphPlan, capture_graph
     torch.manual_seed(8)
@@ -328,5 +355,15 @@ def test_matmul_params_run(cuda, tmp_path):
     from llm_compiler_3_b200.graph import capture_graph
     x = seeded((32, 64), 6, 0.5)
     capture_graph(MatmulParams().half(), (x,), tmp_path)
+    got = _run_twice(tmp_path, [x])[0]
+    _close(got, oracle.run_graph_plan(tmp_path, [x])[0])
+
+
+@pytest.mark.gpu
+def test_layout_preserving_ops_run(cuda, tmp_path):
+    from llm_compiler_3_b200.graph import capture_graph
+    torch.manual_seed(11)
+    x = seeded((2, 8, 64), 12, 0.5)
+    capture_graph(Reshaped().half().eval(), (x,), tmp_path)
     got = _run_twice(tmp_path, [x])[0]
     _close(got, oracle.run_graph_plan(tmp_path, [x])[0])
