@@ -340,7 +340,7 @@ def run_b200(a):
     wall = time.perf_counter() - t0
     e2e_elapsed = max_over_ranks(max(s2.elapsed_time(e2) / 1e3, wall))
 
-    # The north-star case: the same stack and cache at batch 1 (one sequence,
+    # The latency case: the same stack and cache at batch 1 (one sequence,
     # position 4095), through its own captured graph in the same context.
     tok1, pos1, ids1 = tokens[:1].clone(), positions[:1].clone(), ids[:1].clone()
     for _ in range(a.warmup):

@@ -1,7 +1,7 @@
 """Split-KV flash-decoding kernel against the CPU oracle (GPU tests).
 
 Tolerances: FP16 outputs within max-abs 2e-2 and cosine >= 0.9999 of the
-FP32-accumulated oracle; the reference's own SDPA bound
+FP32-accumulated oracle (the FP16 parity bar); the reference's own SDPA bound
 is 2e-2 max-abs (test/Integration/attention.py:99-104,170)."""
 import numpy as np
 import pytest
