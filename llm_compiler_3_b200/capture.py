@@ -26,6 +26,7 @@ decode entry point for transformers' ``LlamaDecoderLayer`` / ``Qwen3DecoderLayer
 """
 from __future__ import annotations
 
+import json
 from pathlib import Path
 from typing import Sequence
 
@@ -109,23 +110,40 @@ def write_decode_capture(step: DecodeStep, config, example: Sequence[torch.Tenso
     """Write the step as the reference's capture directory -- activations first
     (input0 = x, input1 / input2 = the caches, input3 = positions), then every
     parameter and buffer sorted by name, each as arg<N>.bin little-endian --
-    plus a one-layer plan.txt for the runtime.  Returns the plan's path."""
+    plus a one-layer plan.txt for the runtime and a metadata.json describing the
+    package (as npu-compile writes one beside its program,
+    tools/npu-compile/npu-compile.cpp:479-507).  Returns the plan's path."""
     directory = Path(directory)
     directory.mkdir(parents=True, exist_ok=True)
     named = dict(step.named_parameters())
     named.update(dict(step.named_buffers()))
-    lines = []
+    lines, arguments = [], []
     for i, tensor in enumerate(example):
         shape = "x".join(map(str, tensor.shape))
         lines.append(f"{i} input{i} {shape} {str(tensor.dtype).removeprefix('torch.')}")
+        arguments.append({"index": i, "name": f"input{i}", "role": "input",
+                          "shape": list(tensor.shape),
+                          "dtype": str(tensor.dtype).removeprefix("torch."),
+                          "bytes": tensor.numel() * tensor.element_size()})
     for j, name in enumerate(sorted(named), start=len(example)):
         tensor = named[name].detach().contiguous().cpu()
         shape = "x".join(map(str, tensor.shape))
         lines.append(f"{j} {name} {shape} {str(tensor.dtype).removeprefix('torch.')}")
+        arguments.append({"index": j, "name": name, "role": "param", "shape": list(tensor.shape),
+                          "dtype": str(tensor.dtype).removeprefix("torch."),
+                          "bytes": tensor.numel() * tensor.element_size()})
         (directory / f"arg{j}.bin").write_bytes(tensor.numpy().astype(
             tensor.numpy().dtype.newbyteorder("<")).tobytes())
     (directory / "arguments.txt").write_text("\n".join(lines) + "\n")
     batch, capacity = example[0].shape[0], example[1].shape[2]
     plan = DecodePlan.from_hf_config(config, max_batch=max_batch or batch, max_seq=capacity,
                                      layers=1, with_vocab=False)
-    return plan.write(directory / "plan.txt")
+    path = plan.write(directory / "plan.txt")
+    metadata = {"schema": "npu.b200.decode.v1", "stage": "cuda-plan", "numerical_policy": "fp16",
+                "plan": path.name, "arguments": arguments,
+                "outputs": [{"name": "y", "shape": list(example[0].shape)},
+                            {"name": "k_cache", "shape": list(example[1].shape)},
+                            {"name": "v_cache", "shape": list(example[2].shape)}],
+                "param_bytes": sum(a["bytes"] for a in arguments if a["role"] == "param")}
+    (directory / "metadata.json").write_text(json.dumps(metadata, indent=2) + "\n")
+    return path

@@ -104,6 +104,13 @@ def test_capture_directory_layout(tmp_path):
     _native.check(_native.lib().npu_b200_plan_check(str(plan_path).encode(), info, 12))
     assert list(info)[:4] == [1, int(z["shape"][0]), int(z["shape"][1]), int(z["shape"][2])]
     assert info[8] == z["k_cache"].shape[2]
+    import json
+    meta = json.loads((tmp_path / "metadata.json").read_text())
+    assert meta["stage"] == "cuda-plan" and meta["plan"] == "plan.txt"
+    assert [a["name"] for a in meta["arguments"]] == names
+    assert meta["param_bytes"] == sum(
+        (tmp_path / f"arg{a['index']}.bin").stat().st_size for a in meta["arguments"]
+        if a["role"] == "param")
 
 
 @pytest.mark.gpu
