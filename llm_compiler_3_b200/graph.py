@@ -325,3 +325,31 @@ def capture_graph(module: torch.nn.Module, example: Sequence[torch.Tensor],
     }
     (directory / "metadata.json").write_text(json.dumps(metadata, indent=2) + "\n")
     return path
+
+
+def main(argv=None) -> int:
+    """``python -m llm_compiler_3_b200.graph <dir>``: check a graph package on
+    the host with the library's own loader checks (no GPU) and summarise it."""
+    import argparse
+    import ctypes
+
+    from . import _native
+    ap = argparse.ArgumentParser(description=main.__doc__.splitlines()[0])
+    ap.add_argument("directory", type=Path)
+    a = ap.parse_args(argv)
+    out = (ctypes.c_int64 * 6)()
+    try:
+        _native.check(_native.lib().npu_b200_graph_check(str(a.directory).encode(), out, 6))
+    except _native.NpuError as err:
+        print(f"invalid: {err}")
+        return 1
+    plan = GraphPlan.parse((a.directory / "graph.txt").read_text())
+    inputs, outputs, ops, param_bytes, temp_bytes, decode = list(out)
+    print(f"{a.directory}: {inputs} inputs, {outputs} outputs, {ops} ops "
+          f"({', '.join(op[0] for op in plan.ops)}; {decode} as flash-decoding), "
+          f"{param_bytes} parameter bytes, {temp_bytes} temporary bytes")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -263,6 +263,16 @@ def test_unsupported_modules_are_rejected(tmp_path):
         capture_graph(LoneRelu().half(), (seeded((4, 64), 1),), tmp_path / "c")
 
 
+def test_check_command(tmp_path, capsys):
+    from llm_compiler_3_b200.graph import capture_graph, main
+    capture_graph(_mlp(64, 128), (seeded((8, 64), 3),), tmp_path)
+    assert main([str(tmp_path)]) == 0
+    assert "1 inputs, 1 outputs, 2 ops (linear, linear; 0 as flash-decoding)" in capsys.readouterr().out
+    (tmp_path / "arg1.bin").unlink()
+    assert main([str(tmp_path)]) == 1
+    assert "invalid" in capsys.readouterr().out
+
+
 def test_bad_plans_fail_on_the_host(tmp_path):
     from llm_compiler_3_b200 import _native
     from llm_compiler_3_b200.graph import capture_graph
