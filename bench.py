@@ -48,6 +48,8 @@ def parse_args(argv=None):
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--seq", type=int, default=4096, help="keys attended (position + 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the single-GPU attention and layer configs")
     a = ap.parse_args(argv)
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -145,10 +147,26 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def host_cpu_model() -> str:
+    """The host CPU's model name (first entry of /proc/cpuinfo), or the platform's."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
 class CpuOracleStep:
-    """The oracle (PyTorch on the host CPU, FP16 storage, FP32 compute) on a bounded
-    sample of the decode step: one decoder layer and the LM head at the full batch
-    and cache length, extrapolated to the whole stack.  Inputs are built once."""
+    """The oracle (PyTorch on the host CPU, FP16 storage, FP32 compute) running
+    whole decode steps of the stack: the embedding rows, every one of the
+    `layers` decoder layers with its K/V append at the position, the final norm,
+    the LM head and the greedy argmax.  One layer's weights and cache are built
+    once and serve every layer (each layer reads ~1.5 GB, far more than the
+    host's caches hold, so reuse saves memory, not time); the embedding rows are
+    read from the LM-head table (tied embeddings)."""
 
     def __init__(self, batch, layers, seq):
         import torch
@@ -163,45 +181,58 @@ class CpuOracleStep:
         def h(*s, std=0.02):
             return (torch.randn(*s, generator=g) * std).half()
 
+        def norm_w():
+            return (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).half()
+
         self.w = {"self_attn.q_proj.weight": h(HEADS * HEAD_DIM, HIDDEN),
                   "self_attn.k_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
                   "self_attn.v_proj.weight": h(KV_HEADS * HEAD_DIM, HIDDEN),
                   "self_attn.o_proj.weight": h(HIDDEN, HEADS * HEAD_DIM),
                   "mlp.gate_proj.weight": h(FFN, HIDDEN), "mlp.up_proj.weight": h(FFN, HIDDEN),
                   "mlp.down_proj.weight": h(HIDDEN, FFN),
-                  "input_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16),
-                  "post_attention_layernorm.weight": torch.ones(HIDDEN, dtype=torch.float16)}
+                  "input_layernorm.weight": norm_w(),
+                  "post_attention_layernorm.weight": norm_w()}
+        self.final_norm = norm_w()
         self.k = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
         self.v = h(batch, KV_HEADS, seq, HEAD_DIM, std=1.0)
         self.lm = h(VOCAB, HIDDEN)
-        self.x = h(batch, HIDDEN, std=1.0)
+        self.tokens = torch.randint(0, VOCAB, (batch,), generator=g)
         self.pos = torch.full((batch,), seq - 1, dtype=torch.int32)
-        self.sample = (f"oracle: 1 of {layers} layers + LM head at batch {batch}, {seq} keys, "
-                       f"x{layers} layers")
+        self.inv_freq = oracle.rope_inv_freq(self.shape.rope_theta, HEAD_DIM)
+        self.sample = (f"oracle: whole decode steps ({layers} layers with K/V append, final "
+                       f"norm, LM head, argmax) at batch {batch}, {seq} keys")
+
+    def step(self):
+        o, torch = self.oracle, self.torch
+        x = self.lm[self.tokens].float()
+        for _ in range(self.layers):
+            x, _, _ = o.decoder_layer_decode(self.w, x, self.pos, self.k, self.v, self.shape,
+                                             inv_freq=self.inv_freq, write_cache=True)
+        logits = o.linear(o.rms_norm(x, self.final_norm, self.shape.eps), self.lm)
+        return o.greedy_argmax(logits)
 
     def seconds_per_step(self):
-        o, torch = self.oracle, self.torch
         t0 = time.perf_counter()
-        y, _, _ = o.decoder_layer_decode(self.w, self.x, self.pos, self.k, self.v, self.shape,
-                                         write_cache=False)
-        t1 = time.perf_counter()
-        logits = o.linear(o.rms_norm(y, torch.ones(HIDDEN), self.shape.eps), self.lm)
-        o.greedy_argmax(logits)
-        t2 = time.perf_counter()
-        return (t1 - t0) * self.layers + (t2 - t1)
+        self.step()
+        return time.perf_counter() - t0
 
 
 def cpu_baseline(batch, layers, seq, samples=3):
+    """Bounded sample of the CPU oracle: one untimed step, then the median of
+    `samples` whole steps (~4 s each for the 32-layer batch-64 stack on 16 cores)."""
     step = CpuOracleStep(batch, layers, seq)
+    step.seconds_per_step()
     t_step = statistics.median(step.seconds_per_step() for _ in range(samples))
     return {"value": batch / t_step, "unit": "tokens/s", "cores": step.threads, "kind": "port",
-            "sample": f"{step.sample}, median of {samples}", "seconds_per_step": t_step}
+            "sample": f"{step.sample}, median of {samples} after 1 untimed",
+            "cpu_model": host_cpu_model(), "seconds_per_step": t_step}
 
 
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    t_begin = time.perf_counter()
     step = CpuOracleStep(a.batch, a.layers, a.seq)
     times = [step.seconds_per_step() for _ in range(a.warmup + a.steps)][a.warmup:]
     t = statistics.median(times)
@@ -211,11 +242,126 @@ def run_reference(a):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic", "config": workload_config(a),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": step.threads,
-                             "kind": "port", "sample": f"{step.sample}, median of {a.steps}"},
+                             "kind": "port", "cpu_model": host_cpu_model(),
+                             "sample": f"{step.sample}, median of {a.steps} timed steps after "
+                                       f"{a.warmup} untimed"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "timed_s": sum(times), "run_s": time.perf_counter() - t_begin}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def layer_bytes(hidden, heads, kv_heads, ffn, batch, cached, attended, qk_norm=False):
+    """Algorithmic HBM bytes of one decoder-layer decode step (FP16): every weight,
+    `attended` keys of K and V per sequence and KV head, the new K/V entries when
+    `cached` < `attended` counts them apart (cached + 1 = attended), the norms and
+    the layer's input and output rows."""
+    d = HEAD_DIM
+    w = ((heads + 2 * kv_heads) * d * hidden + hidden * heads * d + 3 * ffn * hidden) * 2
+    kv = 2 * batch * kv_heads * cached * d * 2
+    kv_new = 2 * batch * kv_heads * d * 2 if cached < attended else 0
+    norms = 2 * hidden * 2 + (2 * d * 2 if qk_norm else 0)
+    acts = 2 * batch * hidden * 2
+    return w + kv + kv_new + norms + acts
+
+
+def _time_replays(fn, reps, warmup, stream):
+    """Mean seconds per call of `fn` (CUDA events on `stream`, after `warmup` calls)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / 1e3 / reps
+
+
+def measure_configs(dev, peak, warmup, reps=20):
+    """The contract's single-GPU configs 2-4, each through the library's own entry
+    point with inputs resident in HBM, timed with CUDA events; bytes are the
+    configs' algorithmic bytes (FP16, every weight and attended key read once)."""
+    import torch
+    from llm_compiler_3_b200 import ops
+    from llm_compiler_3_b200.plan import llama3_8b, qwen3_8b
+    from llm_compiler_3_b200.runtime import Decoder
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=dev)
+    res = {}
+
+    def randn(shape, seed, std):
+        gen.manual_seed(seed)
+        return (torch.randn(shape, device=dev, generator=gen) * std).half()
+
+    # Config 2: flash-decoding, batch 1, 32 query / 8 KV heads, 4096 keys.  One
+    # launch reads 16.8 MB, less than L2: ten caches are read in turn (168 MB).
+    copies = 10
+    q = randn((1, HEADS, HEAD_DIM), 21, 1.0)
+    kvs = [(randn((1, KV_HEADS, 4096, HEAD_DIM), 22 + 2 * i, 1.0),
+            randn((1, KV_HEADS, 4096, HEAD_DIM), 23 + 2 * i, 1.0)) for i in range(copies)]
+    lens = torch.full((1,), 4096, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    for kc, vc in kvs:
+        ops.flash_decode(q, kc, vc, lens, out=out)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for kc, vc in kvs:
+            ops.flash_decode(q, kc, vc, lens, out=out)
+    t = _time_replays(graph.replay, reps, warmup, stream) / copies
+    b = attention_bytes(1, KV_HEADS, HEADS, 4096)
+    res["attention_b1_kv4096"] = {"us": t * 1e6, "algorithmic_bytes": b,
+                                  "achieved_GBps": b / t / 1e9, "frac": b / t / 1e9 / peak,
+                                  "l2": f"{copies} caches read in turn ({copies * b >> 20} MiB)"}
+    del graph, kvs
+
+    def layer_case(plan, name_shapes, batch, position, qk_norm, seed):
+        with Decoder(plan, device=dev.index) as dec:
+            ones = torch.ones(HIDDEN, dtype=torch.float16, device=dev)
+            for j, (name, shape) in enumerate(name_shapes.items()):
+                dec.set_weight(f"model.layers.0.{name}", randn(shape, seed + j, 0.02))
+            dec.set_weight("model.layers.0.input_layernorm.weight", ones)
+            dec.set_weight("model.layers.0.post_attention_layernorm.weight", ones)
+            if qk_norm:
+                hd = torch.ones(HEAD_DIM, dtype=torch.float16, device=dev)
+                dec.set_weight("model.layers.0.self_attn.q_norm.weight", hd)
+                dec.set_weight("model.layers.0.self_attn.k_norm.weight", hd)
+            k, v = dec.kv_cache(0)
+            gen.manual_seed(seed + 50)
+            k[:batch, :, :position].normal_(generator=gen)
+            v[:batch, :, :position].normal_(generator=gen)
+            x = randn((batch, HIDDEN), seed + 60, 1.0)
+            pos = torch.full((batch,), position, dtype=torch.int32, device=dev)
+            y = torch.empty_like(x)
+            return _time_replays(lambda: dec.forward_hidden_device(x, pos, y), reps, warmup, stream)
+
+    def shapes(ffn):
+        return {"self_attn.q_proj.weight": (HEADS * HEAD_DIM, HIDDEN),
+                "self_attn.k_proj.weight": (KV_HEADS * HEAD_DIM, HIDDEN),
+                "self_attn.v_proj.weight": (KV_HEADS * HEAD_DIM, HIDDEN),
+                "self_attn.o_proj.weight": (HIDDEN, HEADS * HEAD_DIM),
+                "mlp.gate_proj.weight": (ffn, HIDDEN), "mlp.up_proj.weight": (ffn, HIDDEN),
+                "mlp.down_proj.weight": (HIDDEN, ffn)}
+
+    # Config 3: one Llama-3-8B-shaped layer, batch 1, position 2047 (2047 cached keys).
+    t = layer_case(llama3_8b(layers=1, vocab=0, max_batch=1, max_seq=2048), shapes(FFN), 1, 2047,
+                   False, 3000)
+    b = layer_bytes(HIDDEN, HEADS, KV_HEADS, FFN, 1, 2047, 2048)
+    res["llama_layer_b1_pos2047"] = {"us": t * 1e6, "tokens_per_s": 1 / t,
+                                     "algorithmic_bytes": b, "achieved_GBps": b / t / 1e9,
+                                     "frac": b / t / 1e9 / peak}
+    # Config 4: one Qwen3-8B-shaped layer (QK-norm, theta 1e6), batch 16, 8192
+    # keys attended per sequence (8191 cached + the new one).
+    t = layer_case(qwen3_8b(layers=1, vocab=0, max_batch=16, max_seq=8192), shapes(12288), 16,
+                   8191, True, 4000)
+    b = layer_bytes(HIDDEN, HEADS, KV_HEADS, 12288, 16, 8192, 8192, qk_norm=True)
+    res["qwen3_layer_b16_kv8192"] = {"us": t * 1e6, "tokens_per_s": 16 / t,
+                                     "algorithmic_bytes": b, "achieved_GBps": b / t / 1e9,
+                                     "frac": b / t / 1e9 / peak}
+    return res
 
 
 def workload_config(a):
@@ -425,11 +571,14 @@ def run_b200(a):
     }
     if clock_info:
         line["clocks"] = clock_info
+    dec.close()
+    if world == 1 and not a.no_configs:
+        line["configs"] = measure_configs(dev, peak, a.warmup)
     if world == 1 and not a.no_cpu_baseline:
         base = cpu_baseline(a.batch, a.layers, a.seq)
-        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample",
+                                                     "cpu_model")}
     print(json.dumps(line), flush=True)
-    dec.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -112,11 +112,16 @@ NPU_B200_API int npu_b200_flash_decode(const void* d_q, const void* d_k, const v
  * 4 MiB (batch x kv_heads x splits x (8 x head_dim + 16) x 4 bytes plus 64 KiB of
  * counters) is rejected with NPU_B200_E_INVALID.
  *
- * The first call on each device looks up the array's device address (with that
- * device current), so make the first call before any stream capture.  Every call
- * uses the same array and clears the counters it needs before its kernel runs;
- * calls that overlap on the GPU (different streams, or concurrent graphs) race on
- * the array.  Arguments and results are those of npu_b200_flash_decode. */
+ * Each call made outside stream capture looks up the array's device address
+ * (with the calling thread's current device, which must be the device of the
+ * tensors); calls made while `stream` is being captured reuse the address the
+ * last uncaptured call on that device found, so make the first call on each
+ * device before any stream capture (also after cudaDeviceReset, which reloads
+ * the module).  Every call uses the same array and clears the split counters it
+ * needs before its kernel runs; shapes whose splits merge inside one thread-block
+ * cluster (at most 4 sequence x KV-head units, num_splits 0) touch no scratch.
+ * Calls that overlap on the GPU (different streams, or concurrent graphs) race
+ * on the array.  Arguments and results are those of npu_b200_flash_decode. */
 NPU_B200_API int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, const void* d_v,
                                                const int32_t* d_seq_lens, void* d_out, int batch,
                                                int q_heads, int kv_heads, int head_dim,

@@ -51,14 +51,22 @@ def case_proj(a) -> str:
     from . import _native, ops
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
-    w = ops.pack_weight((torch.randn(a.rows, a.k, device=dev, generator=g) * 0.02).half())
+    ws = [ops.pack_weight((torch.randn(a.rows, a.k, device=dev, generator=g) * 0.02).half())
+          for _ in range(max(1, a.copies))]
     x = torch.randn(a.batch, a.k, device=dev, generator=g).half()
     out = torch.empty(a.batch, a.rows, device=dev, dtype=torch.float32)
     e = _native.Epilogue(kind=_native.EPI_STORE, ld_out=a.rows, out_f32=1)
     e.out = out.data_ptr()
-    us = _timed(lambda: ops.projection(x, w, a.rows, e, packed=True), a.repeat, a.graph)
+    turn = [0]
+
+    def call():  # successive launches read successive weight copies
+        ops.projection(x, ws[turn[0] % len(ws)], a.rows, e, packed=True)
+        turn[0] += 1
+
+    us = _timed(call, a.repeat, a.graph)
     gbs = a.rows * a.k * 2 / us / 1e3
-    return f"proj rows={a.rows} k={a.k} batch={a.batch}: {us:.1f} us/launch, {gbs:.0f} GB/s weights"
+    return (f"proj rows={a.rows} k={a.k} batch={a.batch} copies={len(ws)}: {us:.1f} us/launch, "
+            f"{gbs:.0f} GB/s weights")
 
 
 def case_flash(a) -> str:
@@ -157,6 +165,8 @@ def main(argv=None) -> int:
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--repeat", type=int, default=4)
     p.add_argument("--graph", action="store_true", help="time graph replays of the launches")
+    p.add_argument("--copies", type=int, default=1,
+                   help="weight copies read in turn (more than L2 holds: cold weights)")
     f = sub.add_parser("flash")
     f.add_argument("--batch", type=int, default=64)
     f.add_argument("--q-heads", type=int, default=32)

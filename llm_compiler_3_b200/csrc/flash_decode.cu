@@ -505,6 +505,31 @@ int resolve_splits(int batch, int kv_heads, int max_seq, int num_splits, int* kp
   return s;
 }
 
+// The launch shape of one call: key splits per (sequence, KV head), keys per
+// split, and whether the splits of a unit run as one cluster merging through
+// distributed shared memory (then no workspace is used at all).  At most 4
+// units (batch-1 decode of a tensor-parallel shard; the split count left to
+// us): 8 splits per unit as one cluster -- no workspace, no second round trip
+// through L2.  With more units the cluster launch's wait for 8 free SMs of one
+// GPC behind the previous kernel costs more than it saves.
+struct FdLaunch {
+  int splits = 1, kps = 0;
+  bool clustered = false;
+};
+
+FdLaunch plan_fd(int batch, int kv_heads, int max_seq, int num_splits) {
+  FdLaunch L;
+  L.splits = resolve_splits(batch, kv_heads, max_seq, num_splits, &L.kps);
+  if (num_splits == 0 && static_cast<long long>(batch) * kv_heads <= 4 && max_seq > kKeysPerTile) {
+    int kps = (max_seq + 7) / 8;
+    kps = (kps + kKeysPerTile - 1) / kKeysPerTile * kKeysPerTile;
+    L.kps = kps;
+    L.splits = (max_seq + kps - 1) / kps;
+    L.clustered = L.splits > 1;
+  }
+  return L;
+}
+
 size_t workspace_bytes_for(int batch, int kv_heads, int head_dim, int splits) {
   if (splits <= 1) return 0;
   const size_t units = static_cast<size_t>(batch) * kv_heads;
@@ -561,20 +586,9 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
               "flash_decode: q and out must be 4-byte aligned");
   NPU_REQUIRE(num_splits >= 0 && num_splits <= kMaxSplits, "flash_decode: num_splits %d not in [0, %d]",
               num_splits, kMaxSplits);
-  int kps = 0;
-  int splits = resolve_splits(batch, kv_heads, max_seq, num_splits, &kps);
-  // At most 4 (sequence, KV head) units (batch-1 decode of a tensor-parallel
-  // shard; the split count left to us): 8 splits per unit as one cluster,
-  // merged through distributed shared memory -- no workspace, no second
-  // round trip through L2.  With more units the cluster launch's wait for 8
-  // free SMs of one GPC behind the previous kernel costs more than it saves.
-  bool clustered = false;
-  if (num_splits == 0 && static_cast<long long>(batch) * kv_heads <= 4 && max_seq > kKeysPerTile) {
-    kps = (max_seq + 7) / 8;
-    kps = (kps + kKeysPerTile - 1) / kKeysPerTile * kKeysPerTile;
-    splits = (max_seq + kps - 1) / kps;
-    clustered = splits > 1;
-  }
+  const FdLaunch L = plan_fd(batch, kv_heads, max_seq, num_splits);
+  const int kps = L.kps, splits = L.splits;
+  const bool clustered = L.clustered;
   const size_t need = clustered ? 0 : workspace_bytes_for(batch, kv_heads, head_dim, splits);
   NPU_REQUIRE(need == 0 || (workspace && workspace_bytes >= need),
               "flash_decode: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
@@ -604,8 +618,8 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
 
 size_t flash_decode_workspace(int batch, int kv_heads, int head_dim, int max_seq, int num_splits) {
   if (batch < 1 || kv_heads < 1 || max_seq < 1) return 0;
-  const int splits = resolve_splits(batch, kv_heads, max_seq, num_splits, nullptr);
-  return workspace_bytes_for(batch, kv_heads, head_dim, splits);
+  const FdLaunch L = plan_fd(batch, kv_heads, max_seq, num_splits);
+  return L.clustered ? 0 : workspace_bytes_for(batch, kv_heads, head_dim, L.splits);
 }
 
 }  // namespace npu_b200
@@ -644,17 +658,26 @@ std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
 
 // The array's name is only a host-side stand-in for the symbol; the device
-// address differs per device and is looked up once, with that device current.
-int scratch_address(void** out) {
+// address differs per device.  It is looked up with that device current on
+// every call made outside stream capture (so a module reloaded after
+// cudaDeviceReset is found again) and remembered for calls made while `s`
+// is being captured, which must not be the first call on the device.
+int scratch_address(cudaStream_t s, void** out) {
   int dev = 0;
   NPU_TRY_CUDA(cudaGetDevice(&dev));
   NPU_REQUIRE(dev >= 0 && dev < kMaxDevices, "device %d out of range", dev);
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  NPU_TRY_CUDA(cudaStreamIsCapturing(s, &capturing));
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  if (capturing == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     NPU_TRY_CUDA(cudaGetSymbolAddress(&p, g_flash_decode_scratch));
     g_scratch_ptr[dev] = p;
   }
+  NPU_REQUIRE(g_scratch_ptr[dev] != nullptr,
+              "flash_decode_noalloc: the first call on device %d was made during stream capture; "
+              "make one call outside capture first",
+              dev);
   *out = g_scratch_ptr[dev];
   return NPU_B200_OK;
 }
@@ -676,11 +699,11 @@ extern "C" int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, c
               "flash_decode_noalloc: this shape needs %zu bytes of split scratch, more than the "
               "%zu-byte static scratch; use fewer splits or npu_b200_flash_decode",
               need, kNoAllocScratchBytes);
-  void* scratch = nullptr;
-  int rc = scratch_address(&scratch);
-  if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (need > 0) {
+  void* scratch = nullptr;
+  int rc = scratch_address(s, &scratch);
+  if (rc) return rc;
+  if (need > 0) {  // clustered launches merge in shared memory and use no scratch
     // The array keeps whatever the previous call left: the split counters
     // must start at zero.
     const size_t units = static_cast<size_t>(batch) * kv_heads;

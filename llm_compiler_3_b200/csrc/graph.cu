@@ -75,6 +75,10 @@ struct GraphState {
   int64_t param_bytes = 0, temp_bytes = 0;
 };
 
+// Kernel limits mirrored at load time (proj.cu, prefill_attention.cu).
+constexpr long long kLinearMaxTiles = 16384;
+void prefill_blocking(int queries, int group, int* bm, int* hp);
+
 namespace {
 
 int plan_error(const std::string& dir, int line, const char* what) {
@@ -89,7 +93,8 @@ bool parse_dims(const std::string& text, std::vector<int64_t>* dims, int64_t* nu
   while (std::getline(ss, part, 'x')) {
     char* end = nullptr;
     const long long d = strtoll(part.c_str(), &end, 10);
-    if (part.empty() || *end != '\0' || d <= 0 || d > (1ll << 31)) return false;
+    // Every dimension must fit the int arguments of the kernels' entry points.
+    if (part.empty() || *end != '\0' || d <= 0 || d >= (1ll << 31)) return false;
     dims->push_back(d);
     n *= d;
     if (n > (1ll << 40)) return false;
@@ -237,6 +242,8 @@ int parse_graph(const std::string& dir, GraphState* g) {
         op.n = static_cast<int>(tw.dims[0]);
         op.k = static_cast<int>(tw.dims[1]);
         if (op.k % 64 != 0) return plan_error(dir, line, "linear K must be a multiple of 64");
+        if ((static_cast<long long>(op.n) + 127) / 128 > kLinearMaxTiles)
+          return plan_error(dir, line, "linear N exceeds the projection's 2097152 rows");
         if (tx.dims.back() != op.k || tx.numel % op.k != 0)
           return plan_error(dir, line, "linear input's last dimension is not the weight's K");
         op.rows = tx.numel / op.k;
@@ -275,6 +282,13 @@ int parse_graph(const std::string& dir, GraphState* g) {
           return plan_error(dir, line, "sdpa head size must be 32, 64 or 128");
         if (static_cast<long long>(op.batch) * op.kv_heads > 65535)
           return plan_error(dir, line, "sdpa batch x kv_heads exceeds 65535");
+        if (!op.decode) {  // the prefill grid: query blocks x head subgroups in grid.y
+          int bm = 0, hp = 0;
+          prefill_blocking(op.queries, op.heads / op.kv_heads, &bm, &hp);
+          const long long q_blocks = (static_cast<long long>(op.queries) + bm - 1) / bm;
+          if (q_blocks * (op.heads / op.kv_heads / hp) > 65535)
+            return plan_error(dir, line, "sdpa query blocks x head subgroups exceed 65535");
+        }
       } else {
         return plan_error(dir, line, "unknown op (this library runs linear and sdpa)");
       }

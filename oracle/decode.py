@@ -36,7 +36,8 @@ from typing import Callable, Mapping
 import torch
 
 __all__ = [
-    "DecoderShape", "grid_values", "linear", "rms_norm", "rope_inv_freq", "rope_cos_sin",
+    "DecoderShape", "grid_values", "linear", "rms_norm", "norm_for_projection", "rope_inv_freq",
+    "rope_cos_sin",
     "apply_rope", "attention_decode", "attention_prefill", "attention_online", "silu_mul", "decoder_layer_decode",
     "stack_decode", "mlp_forward", "greedy_argmax", "cosine", "LLAMA3_8B", "QWEN3_8B",
 ]
@@ -211,10 +212,29 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.silu(gate) * up
 
 
+def _handoff(t: torch.Tensor, fp16: bool) -> torch.Tensor:
+    """A tensor handed from one kernel to the next: stored in FP16 when `fp16`."""
+    return t.to(torch.float16).to(torch.float32) if fp16 else t
+
+
+def norm_for_projection(x: torch.Tensor, weight: torch.Tensor, eps: float,
+                        fp16: bool = False) -> torch.Tensor:
+    """RMSNorm of a projection's input.  With fp16, as the B200 kernels hand it
+    over: the producer stores xw = fp16(x * w) and the consumer multiplies its
+    FP32 dot products by rsqrt(mean(x^2) + eps) (linear in the row, so the scale
+    is applied here before the product)."""
+    if not fp16:
+        return rms_norm(x, weight, eps)
+    x = x.to(torch.float32)
+    scale = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    return scale * _handoff(x * _f32(weight), True)
+
+
 def decoder_layer_decode(weights: Mapping[str, torch.Tensor], x: torch.Tensor,
                          positions: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                          shape: DecoderShape, inv_freq: torch.Tensor | None = None,
-                         write_cache: bool = True) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+                         write_cache: bool = True, fp16_handoff: bool = False
+                         ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """One decode step of LlamaDecoderLayer / Qwen3DecoderLayer for B sequences.
 
     weights: transformers names relative to the layer ("self_attn.q_proj.weight", ...).
@@ -222,6 +242,13 @@ def decoder_layer_decode(weights: Mapping[str, torch.Tensor], x: torch.Tensor,
     Sequence b writes its new K/V at positions[b] and attends keys [0, positions[b]].
     Returns (y FP32 [B, hidden], k_new FP32 [B, Hkv, D], v_new FP32 [B, Hkv, D]); with
     write_cache the FP16-rounded new entries are stored into the caches in place.
+
+    fp16_handoff rounds to FP16 where the B200 path stores a tensor between
+    kernels -- the normed projection inputs (norm_for_projection), q / k / v
+    after RoPE (k and v are attended from the FP16 cache), the attention output
+    and the SwiGLU output -- so that only accumulation order differs; the
+    residual stream stays FP32 as there.  Off, every intermediate is FP32 (the
+    FP32-accumulated result the tolerances refer to).
     """
     batch = x.shape[0]
     hd = shape.head_dim
@@ -229,7 +256,7 @@ def decoder_layer_decode(weights: Mapping[str, torch.Tensor], x: torch.Tensor,
         inv_freq = rope_inv_freq(shape.rope_theta, hd)
     x = x.to(torch.float32)
     residual = x
-    h = rms_norm(x, weights["input_layernorm.weight"], shape.eps)
+    h = norm_for_projection(x, weights["input_layernorm.weight"], shape.eps, fp16_handoff)
     q = linear(h, weights["self_attn.q_proj.weight"]).view(batch, shape.heads, hd)
     k = linear(h, weights["self_attn.k_proj.weight"]).view(batch, shape.kv_heads, hd)
     v = linear(h, weights["self_attn.v_proj.weight"]).view(batch, shape.kv_heads, hd)
@@ -237,8 +264,9 @@ def decoder_layer_decode(weights: Mapping[str, torch.Tensor], x: torch.Tensor,
         q = rms_norm(q, weights["self_attn.q_norm.weight"], shape.eps)
         k = rms_norm(k, weights["self_attn.k_norm.weight"], shape.eps)
     cos, sin = rope_cos_sin(inv_freq, positions)
-    q = apply_rope(q, cos, sin)
-    k = apply_rope(k, cos, sin)
+    q = _handoff(apply_rope(q, cos, sin), fp16_handoff)
+    k = _handoff(apply_rope(k, cos, sin), fp16_handoff)
+    v = _handoff(v, fp16_handoff)
 
     attn = torch.zeros(batch, shape.heads, hd)
     scale = hd ** -0.5
@@ -253,12 +281,15 @@ def decoder_layer_decode(weights: Mapping[str, torch.Tensor], x: torch.Tensor,
             k_cache[b, :, p] = k[b].to(k_cache.dtype)
             v_cache[b, :, p] = v[b].to(v_cache.dtype)
 
+    attn = _handoff(attn, fp16_handoff)
     y = residual + linear(attn.reshape(batch, -1), weights["self_attn.o_proj.weight"])
     residual = y
-    h = rms_norm(y, weights["post_attention_layernorm.weight"], shape.eps)
+    h = norm_for_projection(y, weights["post_attention_layernorm.weight"], shape.eps,
+                            fp16_handoff)
     gate = linear(h, weights["mlp.gate_proj.weight"])
     up = linear(h, weights["mlp.up_proj.weight"])
-    y = residual + linear(silu_mul(gate, up), weights["mlp.down_proj.weight"])
+    act = _handoff(silu_mul(gate, up), fp16_handoff)
+    y = residual + linear(act, weights["mlp.down_proj.weight"])
     return y, k, v
 
 
@@ -266,19 +297,20 @@ def stack_decode(layer_weights: Callable[[int], Mapping[str, torch.Tensor]], num
                  embed: torch.Tensor, final_norm: torch.Tensor, lm_head: torch.Tensor,
                  tokens: torch.Tensor, positions: torch.Tensor,
                  caches: Callable[[int], tuple[torch.Tensor, torch.Tensor]],
-                 shape: DecoderShape, return_logits: bool = False):
+                 shape: DecoderShape, return_logits: bool = False, fp16_handoff: bool = False):
     """LlamaForCausalLM decode step followed by greedy argmax.
 
     layer_weights(i) / caches(i) produce layer i's tensors on demand, so a 32-layer
     8B-shaped stack is checked one layer at a time.  Returns argmax ids [B]
-    (ties to the lowest id, like torch.argmax) and, if asked, FP32 logits."""
+    (ties to the lowest id, like torch.argmax) and, if asked, FP32 logits.
+    fp16_handoff as in decoder_layer_decode (the LM head's input included)."""
     inv_freq = rope_inv_freq(shape.rope_theta, shape.head_dim)
     x = _f32(embed[tokens.long()])
     for i in range(num_layers):
         k_cache, v_cache = caches(i)
         x, _, _ = decoder_layer_decode(layer_weights(i), x, positions, k_cache, v_cache, shape,
-                                       inv_freq=inv_freq)
-    h = rms_norm(x, final_norm, shape.eps)
+                                       inv_freq=inv_freq, fp16_handoff=fp16_handoff)
+    h = norm_for_projection(x, final_norm, shape.eps, fp16_handoff)
     logits = linear(h, lm_head)
     ids = greedy_argmax(logits)
     return (ids, logits) if return_logits else ids

@@ -32,6 +32,10 @@ def test_reference_arm_json_line():
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s",
                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert line["cpu_baseline"]["cpu_model"]
+    # Whole steps were run, not extrapolated: the timed steps fit in the run.
+    assert line["steps"] * line["ms_per_step"] / 1e3 <= line["timed_s"] * 1.001
+    assert line["timed_s"] <= line["run_s"]
 
 
 def test_reference_arm_under_torchrun_prints_once():

@@ -5,6 +5,7 @@ changes; greedy token ids.  Toleranced: FP16 outputs within max-abs 2e-2 and
 cosine >= 0.9999 of the FP32-accumulated oracle."""
 import os
 import tempfile
+import warnings
 from pathlib import Path
 
 import numpy as np
@@ -206,16 +207,18 @@ def test_stack_argmax_two_layers(cuda):
     ref_ids, logits = oracle.stack_decode(
         lambda i: per_layer[i], layers, top["model.embed_tokens.weight"], top["model.norm.weight"],
         top["lm_head.weight"], tokens, positions,
-        lambda i: (caches[i][0].clone(), caches[i][1].clone()), shape, return_logits=True)
+        lambda i: (caches[i][0].clone(), caches[i][1].clone()), shape, return_logits=True,
+        fp16_handoff=True)
     _check_ids(ids, ref_ids, logits)
 
 
 def _check_ids(ids, ref_ids, logits):
     """Greedy ids must equal the oracle's wherever the oracle's top-2 logit gap
-    exceeds the error the FP16 intermediates can cause (about 1e-3 of the logit
-    scale here: every projection input is an FP16 tensor); closer pairs are
-    near-ties, reported with their gap, and may only differ by picking the
-    runner-up."""
+    exceeds what accumulation order alone can move (4e-3 of the logit standard
+    deviation; the oracle given here rounds at the kernels' FP16 hand-offs
+    wherever a caller can, so only summation order differs).  A closer pair is a
+    near-tie: it may only pick the oracle's runner-up, and every such flip is
+    reported as a warning with its gap.  Returns the number of flips."""
     ids = np.asarray(ids)
     ref = ref_ids.numpy()
     top2 = logits.topk(2, dim=-1)
@@ -227,7 +230,10 @@ def _check_ids(ids, ref_ids, logits):
             f"sequence {b}: id {ids[b]} != oracle {ref[b]} with top-2 gap {gaps[b]:.3e} "
             f">= bound {tie_bound:.3e}")
         assert ids[b] == int(top2.indices[b, 1]), f"sequence {b}: not the oracle's runner-up"
+        warnings.warn(f"near-tie flip, sequence {b}: id {ids[b]} is the oracle's runner-up "
+                      f"(oracle {ref[b]}), top-2 gap {gaps[b]:.3e} < bound {tie_bound:.3e}")
     assert len(mism) <= max(1, len(ids) // 16), f"{len(mism)} near-tie flips of {len(ids)}"
+    return len(mism)
 
 
 def test_decode_errors_are_status_codes(cuda):
@@ -299,5 +305,6 @@ def test_stack_config_full_size(cuda):
         ref_ids, logits = oracle.stack_decode(
             lambda i: {n: t.cpu() for n, t in layer(i).items()}, layers, embed.cpu(), norm.cpu(),
             lm.cpu(), tokens.cpu(), positions,
-            lambda i: tuple(t.cpu() for t in dec.kv_cache(i)), shape, return_logits=True)
+            lambda i: tuple(t.cpu() for t in dec.kv_cache(i)), shape, return_logits=True,
+            fp16_handoff=True)
     _check_ids(ids, ref_ids, logits)

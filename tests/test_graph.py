@@ -298,6 +298,18 @@ def test_bad_plans_fail_on_the_host(tmp_path):
           "never written")
     check(text.replace("tensor linear temp f16 8x128", "tensor linear temp f16 8x64"),
           "not \\[rows, N\\]")
+    # Dimensions must fit the kernels' int arguments (2^31 does not).
+    check(text.replace("tensor linear temp f16 8x128", "tensor linear temp f16 8x2147483648"),
+          "bad dimensions")
+    # The projection's row limit (16384 tiles of 128 rows), checked at load:
+    # a weight given as an input needs no parameter file of that size.
+    head = "npu.stage cuda-graph\nnpu.schema 1\n"
+    check(head + "tensor x input f16 8x64\ntensor w input f16 2097280x64\n"
+          "tensor y output f16 8x2097280\nop linear y x w - 0\n", "2097152 rows")
+    # The prefill grid: query blocks x head subgroups in one grid dimension.
+    check(head + "tensor q input f16 1x1x8388736x32\ntensor k input f16 1x1x16x32\n"
+          "tensor v input f16 1x1x16x32\ntensor o output f16 1x1x8388736x32\n"
+          "op sdpa o q k v 0.17677669 1\n", "query blocks")
     (tmp_path / "graph.txt").unlink()
     with pytest.raises(_native.NpuError, match="cannot read"):
         _check_info(tmp_path)

@@ -102,3 +102,34 @@ def test_argmax_ties_break_low():
     logits = torch.tensor([[1.0, 3.0, 3.0, 2.0], [5.0, 5.0, 5.0, 5.0]])
     assert oracle.greedy_argmax(logits).tolist() == [1, 0]
     assert torch.equal(oracle.greedy_argmax(logits), torch.argmax(logits, dim=-1))
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen3"])
+def test_fp16_handoff_variant_stays_within_tolerance(family):
+    """The variant that rounds where the kernels hand tensors over in FP16 is the
+    same layer to within the FP16 tolerance, yet not the FP32 result itself."""
+    z = _load(f"{family}_layer_decode.npz")
+    hidden, heads, kv, hd, ffn = (int(v) for v in z["shape"])
+    shape = oracle.DecoderShape(hidden=hidden, heads=heads, kv_heads=kv, head_dim=hd, ffn=ffn,
+                                eps=float(z["eps"]), rope_theta=float(z["rope_theta"]),
+                                qk_norm=family == "qwen3")
+    weights = {k[2:]: torch.from_numpy(v) for k, v in z.items() if k.startswith("w.")}
+    positions = torch.from_numpy(z["positions"])
+    runs = [oracle.decoder_layer_decode(weights, torch.from_numpy(z["x"]), positions,
+                                        torch.from_numpy(z["k_cache"]).clone(),
+                                        torch.from_numpy(z["v_cache"]).clone(), shape,
+                                        fp16_handoff=h) for h in (False, True)]
+    (y32, k32, _), (y16, k16, _) = runs
+    assert float((y16 - torch.from_numpy(z["expected_y"])).abs().max()) < 2e-2
+    assert oracle.cosine(y16, torch.from_numpy(z["expected_y"])) >= 0.9999
+    assert not torch.equal(y16, y32)
+    assert torch.equal(k16, k16.half().float())  # new keys leave in FP16
+
+
+def test_norm_for_projection_scales_after_rounding():
+    x = torch.tensor([[3.0, 4.0, 0.001, -2.0]])
+    w = torch.tensor([1.0, 0.5, 2.0, 1.5]).half()
+    scale = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-5)
+    expected = scale * (x * w.float()).half().float()
+    assert torch.equal(oracle.norm_for_projection(x, w, 1e-5, fp16=True), expected)
+    assert torch.equal(oracle.norm_for_projection(x, w, 1e-5), oracle.rms_norm(x, w, 1e-5))

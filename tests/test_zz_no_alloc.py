@@ -34,21 +34,28 @@ def _noalloc(q, k, v, lens, num_splits=0):
 
 
 @pytest.mark.parametrize("batch,seq,lens,splits", [
-    (1, 4096, [4096], 0),              # the flash-decoding config: 16 splits
+    (1, 4096, [4096], 0),              # the flash-decoding config: split count chosen by the library
+    (4, 4096, [4096, 3000, 1, 2048], 0),  # chosen splits merged through the static scratch
     (4, 1000, [1000, 1, 517, 0], 5),   # ragged lengths, an empty sequence
 ])
 def test_noalloc_matches_allocating_entry(cuda, batch, seq, lens, splits):
+    """Two calls in a row: each must match the allocating entry point and the
+    CPU oracle within the flash-decoding tolerance."""
     from llm_compiler_3_b200 import _native, ops
     dev = torch.device("cuda", 0)
-    q = seeded((batch, 32, 128), 61).to(dev)
-    k = seeded((batch, 8, seq, 128), 62).to(dev)
-    v = seeded((batch, 8, seq, 128), 63).to(dev)
+    q_h = seeded((batch, 32, 128), 61)
+    k_h = seeded((batch, 8, seq, 128), 62)
+    v_h = seeded((batch, 8, seq, 128), 63)
+    q, k, v = q_h.to(dev), k_h.to(dev), v_h.to(dev)
     lens_d = torch.tensor(lens, dtype=torch.int32, device=dev)
-    expected = ops.flash_decode(q, k, v, lens_d, num_splits=splits).float()
+    expected = ops.flash_decode(q, k, v, lens_d, num_splits=splits).float().cpu()
+    ref = oracle.attention_decode(q_h, k_h, v_h, lens, 128 ** -0.5)
     for _ in range(2):  # the second call sees the scratch the first one left
-        got = _noalloc(q, k, v, lens_d, splits).float()
+        got = _noalloc(q, k, v, lens_d, splits).float().cpu()
         assert float((got - expected).abs().max()) <= ATOL
-        assert oracle.cosine(got.cpu(), expected.cpu()) >= 0.9999
+        assert oracle.cosine(got, expected) >= 0.9999
+        assert float((got - ref).abs().max()) <= ATOL
+        assert oracle.cosine(got, ref) >= 0.9999
     assert _native.device_status() == 0
 
 
