@@ -345,7 +345,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* fixbar = drain + 1;  // stream-K owner: other contributors' partials landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fixbar + 1);
   // Per-token scalars, padded by one chunk so a chunk starting anywhere below
   // BN may read 16 entries.
   float* rn = reinterpret_cast<float*>(tmem_slot + 4);          // [BN+16] RMSNorm scale
@@ -388,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       mbar_init(&tempty[a], kEpiThreads);
     }
     mbar_init(drain, 1);
+    mbar_init(fixbar, 1);
     flags[0] = 0;
     flags[1] = 0;
     fence_barrier_init();
@@ -515,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
     epi_sync();
     long long it = it_begin;
-    int seg = 0;
+    int seg = 0, fix_uses = 0;
     if (clustered) {
       // One segment: publish the FP32 partial in this CTA's own shared memory
       // (the pipeline stages are idle once every MMA has completed).
@@ -564,10 +566,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
-      } else {
-        // Stream-K fix-up: publish this CTA's partial (slot tile + cta is
-        // unique), release the accumulator, and let the last contributor of
-        // the tile add every partial in CTA order (deterministic).
+      } else if (kb0 != 0) {
+        // Stream-K, a later part of a tile (the first segment of this CTA's
+        // range, so it finishes early): publish this CTA's FP32 partial (slot
+        // tile + cta is unique), release the accumulator and count the partial
+        // for the tile's owner.
         float* slot = slots + static_cast<size_t>(tile + cta) * 128 * BN;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
@@ -581,41 +584,74 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         mbar_arrive(&tempty[acc]);
         __threadfence();
         epi_sync();
-        const int cf = owner_cta(static_cast<long long>(tile) * kblocks, total, grid);
+        if (r == 0) atomicAdd(&counters[tile], 1u);
+      } else {
+        // Stream-K, the head of a tile whose later k-blocks other CTAs hold
+        // (always the last segment of this CTA's range, so the ring is idle):
+        // wait until their partials are counted, bring them into the ring with
+        // bulk copies (one round trip), add them to this CTA's accumulator in
+        // CTA order -- the order of the k-blocks, so the sum is deterministic
+        // -- and run the epilogue.  Partials that do not fit the ring are read
+        // from L2 chunk by chunk instead.
+        constexpr uint32_t kPartBytes = 128u * BN * 4u;
         const int cl = owner_cta(static_cast<long long>(tile + 1) * kblocks - 1, total, grid);
+        const int n_other = cl - cta;
+        const bool staged = n_other * kPartBytes <= static_cast<uint32_t>(stages) * S::kStageBytes;
+        bool bad = false;
         if (r == 0) {
-          const uint32_t prev = atomicAdd(&counters[tile], 1u);
-          flags[1] = (prev == static_cast<uint32_t>(cl - cf)) ? 1 : 0;
-        }
-        epi_sync();
-        if (flags[1]) {
-          __threadfence();
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
-            float v[kChunkCols];
-#pragma unroll
-            for (int q = 0; q < kChunkCols; ++q) v[q] = 0.f;
-            // Loads of up to 4 contributors in flight together; sums in CTA order.
-            for (int c = cf; c <= cl; c += 4) {
-              float t[4][kChunkCols];
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const float* other =
-                    slots + static_cast<size_t>(tile + c + u) * 128 * BN + c0 * 128 + r;
-#pragma unroll
-                for (int q = 0; q < kChunkCols; ++q)
-                  t[u][q] = c + u <= cl ? __ldcg(other + q * 128) : 0.f;
-              }
-#pragma unroll
-              for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int q = 0; q < kChunkCols; ++q) v[q] += t[u][q];
-            }
-            run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
+          bool ready = false;
+          for (uint32_t i = 0; i < kMaxPolls && !ready; ++i) {
+            ready = ld_acquire_gpu(counters + tile) >= static_cast<uint32_t>(n_other);
+            if (!ready) __nanosleep(32);
           }
-          if (r == 0) counters[tile] = 0u;  // leave the workspace reusable
+          if (!ready) report_error(kDevErrEpilogueTimeout);
+          bad = !ready;
+          if (ready && staged) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_arrive_expect_tx(fixbar, n_other * kPartBytes);
+            for (int u = 0; u < n_other; ++u)
+              bulk_load(smem + u * kPartBytes, slots + static_cast<size_t>(tile + cta + 1 + u) * 128 * BN,
+                        kPartBytes, fixbar);
+          }
         }
-        epi_sync();  // flags[1] is rewritten by the next fix-up
+        bad = epi_sync_or(bad);
+        if (!bad && staged) bad = epi_sync_or(!mbar_wait(fixbar, fix_uses & 1, kDevErrTmaTimeout));
+        ++fix_uses;
+        if (bad) {
+          flags[0] = 1;
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+          break;
+        }
+        __threadfence();
+        const float* parts = reinterpret_cast<const float*>(smem);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
+          uint32_t rr[16];
+          tmem_ld16(taddr + c0, rr);
+          tmem_ld_wait();
+          float v[kChunkCols];
+#pragma unroll
+          for (int q = 0; q < kChunkCols; ++q) v[q] = __uint_as_float(rr[q]);
+          for (int u = 0; u < n_other; ++u) {
+            float t[kChunkCols];
+            if (staged) {
+              const float* src = parts + static_cast<size_t>(u) * 128 * BN + c0 * 128 + r;
+#pragma unroll
+              for (int q = 0; q < kChunkCols; ++q) t[q] = src[q * 128];
+            } else {
+              const float* src = slots + static_cast<size_t>(tile + cta + 1 + u) * 128 * BN + c0 * 128 + r;
+#pragma unroll
+              for (int q = 0; q < kChunkCols; ++q) t[q] = __ldcg(src + q * 128);
+            }
+#pragma unroll
+            for (int q = 0; q < kChunkCols; ++q) v[q] += t[q];
+          }
+          run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        if (r == 0) counters[tile] = 0u;  // leave the workspace reusable
       }
       it = seg_end;
       ++seg;

@@ -60,6 +60,11 @@ import torch
 STAGE = "cuda-graph"
 SCHEMA = 1
 
+# Ops that become aliases of their source (no kernel, no copy).  clone and
+# contiguous are among them: this is sound only because no op of a plan writes
+# its operands in place and an output must be computed by an op (an alias of
+# an input, or of another output, is refused when the outputs are bound), so an
+# alias never shares bytes with a tensor that is written after it is read.
 _VIEWS = {"aten.view.default", "aten.reshape.default", "aten.contiguous.default",
           "aten.clone.default", "aten._unsafe_view.default", "aten.alias.default",
           "aten.flatten.using_ints", "aten.unsqueeze.default", "aten.squeeze.dim",

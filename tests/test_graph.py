@@ -262,6 +262,26 @@ def test_unsupported_modules_are_rejected(tmp_path):
     with pytest.raises(GraphUnsupported):
         capture_graph(LoneRelu().half(), (seeded((4, 64), 1),), tmp_path / "c")
 
+    # clone / contiguous become aliases: an output that is only a copy of an
+    # input (or of another output) would share its bytes, so it is refused.
+    class CloneOut(torch.nn.Module):
+        def forward(self, x):
+            return x.clone()
+
+    class ContiguousTwice(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.lin = torch.nn.Linear(64, 64)
+
+        def forward(self, x):
+            y = self.lin(x)
+            return y, y.contiguous()
+
+    with pytest.raises(GraphUnsupported, match="not computed by an op"):
+        capture_graph(CloneOut(), (seeded((4, 64), 1),), tmp_path / "e")
+    with pytest.raises(GraphUnsupported, match="returned twice"):
+        capture_graph(ContiguousTwice().half(), (seeded((4, 64), 1),), tmp_path / "f")
+
 
 def test_check_command(tmp_path, capsys):
     from llm_compiler_3_b200.graph import capture_graph, main
