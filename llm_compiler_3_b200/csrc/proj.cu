@@ -519,8 +519,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     long long it = it_begin;
     int seg = 0, fix_uses = 0;
     if (clustered) {
-      // One segment: publish the FP32 partial in this CTA's own shared memory
-      // (the pipeline stages are idle once every MMA has completed).
+      // One segment: keep the FP32 partial in this CTA's own shared memory
+      // (the pipeline stages are idle once every MMA has completed) and, when
+      // the members reduce through L2 (mode 2), also in this CTA's workspace
+      // slot, token by token (128 rows of a token are 512 contiguous bytes).
       const bool bad = flags[0] || !mbar_wait(&tfull[0], 0, kDevErrMmaTimeout);
       if (epi_sync_or(bad)) {
         flags[0] = 1;
@@ -528,15 +530,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
         float* red = reinterpret_cast<float*>(smem);
+        const int pitch = clustered == 2 ? 128 : S::kPitch;
+        float* slot = clustered == 2 ? slots + static_cast<size_t>(cta) * 128 * BN : nullptr;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += kChunkCols) {
           uint32_t rr[16];
           tmem_ld16(taddr + c0, rr);
           tmem_ld_wait();
 #pragma unroll
-          for (int q = 0; q < kChunkCols; ++q) red[(c0 + q) * S::kPitch + r] = __uint_as_float(rr[q]);
+          for (int q = 0; q < kChunkCols; ++q) {
+            const float x = __uint_as_float(rr[q]);
+            red[(c0 + q) * pitch + r] = x;
+            if (slot != nullptr) __stcg(slot + (c0 + q) * 128 + r, x);
+          }
         }
         tc_fence_before();
+        if (slot != nullptr) __threadfence();
       }
       it = it_end;  // skip the stream-K loop
     }
@@ -659,9 +668,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
 
   if (clustered) {
-    // Cross-CTA reduction through distributed shared memory: member j sums the
-    // partials of every member, in rank order, for its share of the tokens and
-    // runs the epilogue on them.
+    // Cross-CTA reduction: member j sums the partials of every member, in rank
+    // order, for its share of the tokens and runs the epilogue on them.  Mode
+    // 2: the partials are in L2 (each member's workspace slot, published before
+    // the cluster barrier); member j brings its tokens of every other member's
+    // partial into its idle ring with one bulk copy each -- one round trip.
+    // Mode 1 (when those do not fit the ring): member j reads them from the
+    // peers' shared memory.
     cluster_sync_all();
     if (warp < 4) {
       const int r = threadIdx.x;
@@ -669,7 +682,47 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       const int c_begin = static_cast<int>(static_cast<long long>(crank) * ep.batch / csize);
       const int c_end = static_cast<int>(static_cast<long long>(crank + 1) * ep.batch / csize);
       const uint32_t red0 = smem_u32(smem);
-      const bool ok = !epi_sync_or(flags[0] != 0);
+      bool ok = !epi_sync_or(flags[0] != 0);
+      if (clustered == 2) {
+        constexpr uint32_t kTokBytes = 128 * 4;
+        const int n_tok = c_end - c_begin;
+        uint8_t* recv = smem + BN * kTokBytes;  // [other member][n_tok][128] after the partial
+        const bool fetch = ok && n_tok > 0 && csize > 1;
+        if (fetch && r == 0) {
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          mbar_arrive_expect_tx(fixbar, (csize - 1) * n_tok * kTokBytes);
+          int j = 0;
+          for (uint32_t m = 0; m < csize; ++m) {
+            if (m == crank) continue;
+            const float* src = slots + static_cast<size_t>(cta - crank + m) * 128 * BN +
+                               static_cast<size_t>(c_begin) * 128;
+            bulk_load(recv + static_cast<size_t>(j) * n_tok * kTokBytes, src, n_tok * kTokBytes,
+                      fixbar);
+            ++j;
+          }
+        }
+        const bool landed = !fetch || mbar_wait(fixbar, 0, kDevErrTmaTimeout);
+        ok = !epi_sync_or(!ok || !landed);
+        const float* own = reinterpret_cast<const float*>(smem);
+        const float* got = reinterpret_cast<const float*>(recv);
+        for (int b0 = c_begin; ok && b0 < c_end; b0 += kChunkCols) {
+          float v[kChunkCols];
+#pragma unroll
+          for (int q = 0; q < kChunkCols; ++q) v[q] = 0.f;
+          int j = 0;
+          for (uint32_t m = 0; m < csize; ++m) {
+            const float* src = m == crank
+                                   ? own + static_cast<size_t>(b0) * 128 + r
+                                   : got + (static_cast<size_t>(j) * n_tok + (b0 - c_begin)) * 128 + r;
+#pragma unroll
+            for (int q = 0; q < kChunkCols; ++q)
+              if (b0 + q < c_end) v[q] += src[q * 128];
+            if (m != crank) ++j;
+          }
+          run_epilogue_chunk(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
+        }
+        ok = false;  // done: the shared-memory pull below is for mode 1
+      }
       for (int b0 = c_begin; ok && b0 < c_end; b0 += kChunkCols) {
         float v[kChunkCols];
 #pragma unroll
@@ -695,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         run_epilogue_chunk(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
       }
     }
-    cluster_sync_all();  // no CTA leaves while a peer may still read its partial
+    if (clustered == 1) cluster_sync_all();  // no CTA leaves while a peer may still read its partial
   }
   tc_fence_before();
   __syncthreads();
@@ -782,8 +835,19 @@ int max_clusters(int bn, int s) {
 struct Geometry {
   int bn, n_tiles, kblocks, grid;
   int split;       // > 0: clustered split-K with `split` CTAs per tile; 0: stream-K
+  int mode;        // kernel's `clustered`: 0 stream-K, 1 reduce in shared memory, 2 through L2
   size_t counter_bytes, slot_bytes;
 };
+
+// Bytes of proj_kernel<bn>'s ring (idle once the k-loop is done).
+size_t ring_bytes(int bn) {
+  switch (bn) {
+    case 16: return static_cast<size_t>(stages_for<16>()) * ProjShape<16>::kStageBytes;
+    case 32: return static_cast<size_t>(stages_for<32>()) * ProjShape<32>::kStageBytes;
+    case 64: return static_cast<size_t>(stages_for<64>()) * ProjShape<64>::kStageBytes;
+    default: return static_cast<size_t>(stages_for<128>()) * ProjShape<128>::kStageBytes;
+  }
+}
 
 // Few tiles (fewer than one per CTA slot): split each tile's K over a cluster
 // and reduce through distributed shared memory -- no global scratch, no
@@ -805,11 +869,19 @@ Geometry geometry(int n_rows, int k, int batch) {
       if (g.n_tiles <= max_clusters(g.bn, s)) best = s;
     g.split = best;
     g.grid = g.n_tiles * best;
-    g.counter_bytes = 0;
-    g.slot_bytes = 0;
+    // Through L2 when the member's partial and its tokens of the others'
+    // partials fit the ring; each member then needs a workspace slot.
+    const size_t tok_max = (static_cast<size_t>(batch) + best - 1) / best;
+    const size_t staged = static_cast<size_t>(g.bn) * 512 + (best - 1) * tok_max * 512;
+    g.mode = best > 1 && staged <= ring_bytes(g.bn) ? 2 : 1;
+    // The slots start after the stream-K counters, which a workspace shared
+    // between projections must keep zero-filled.
+    g.counter_bytes = g.mode == 2 ? kCounterBytes : 0;
+    g.slot_bytes = g.mode == 2 ? static_cast<size_t>(g.grid) * 128 * g.bn * 4 : 0;
     return g;
   }
   g.grid = static_cast<int>(total < slots_total ? total : slots_total);
+  g.mode = 0;
   g.counter_bytes = kCounterBytes;
   g.slot_bytes = static_cast<size_t>(g.n_tiles + g.grid - 1) * 128 * g.bn * 4;
   return g;
@@ -831,8 +903,8 @@ int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& e
   cfg.stream = stream;
   cfg.pdl = pdl;
   cfg.cluster = g.split > 1 ? g.split : 1;
-  return launch(cfg, kern, wm, xm, ep, w_packed, g.n_tiles, g.kblocks, stages,
-                g.split > 0 ? 1 : 0, slots, counters);
+  return launch(cfg, kern, wm, xm, ep, w_packed, g.n_tiles, g.kblocks, stages, g.mode, slots,
+                counters);
 }
 
 // One thread per 16-byte chunk of the source: row i, chunk c (elements 8c..8c+7)
