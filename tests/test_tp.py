@@ -90,8 +90,9 @@ def _rank_main(rank, world, port, out_dir):
     from llm_compiler_3_b200.runtime import Decoder, nccl_unique_id
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
+    import datetime
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
-                            world_size=world)
+                            world_size=world, timeout=datetime.timedelta(seconds=300))
     s = SHAPE
     plan = DecodePlan(arch="llama", hidden=s.hidden, heads=s.heads, kv_heads=s.kv_heads,
                       head_dim=s.head_dim, ffn=s.ffn, layers=s.layers, vocab=s.vocab,
