@@ -119,9 +119,19 @@ def case_step(a) -> str:
     from . import _native
     from .plan import llama3_8b
     from .runtime import Decoder
-    H, V, F = 4096, 128256, 14336
+    from .plan import DecodePlan
+    # --shard N: one tensor-parallel rank's share of a TP=N run (its heads, FFN
+    # columns and vocabulary rows) as a one-GPU plan -- the same kernels at the
+    # same shapes, without the exchanges.
+    n = a.shard
+    H, V, F = 4096, -(-128256 // n), 14336 // n
+    Q, KV = 32 // n, 8 // n
     dev = torch.device("cuda", 0)
-    dec = Decoder(llama3_8b(layers=a.layers, max_batch=a.batch, max_seq=a.seq), device=0)
+    plan = llama3_8b(layers=a.layers, max_batch=a.batch, max_seq=a.seq) if n == 1 else \
+        DecodePlan(arch="llama", hidden=H, heads=Q, kv_heads=KV, head_dim=128, ffn=F,
+                   layers=a.layers, vocab=V, rms_eps=1e-5, rope_theta=500000.0,
+                   max_batch=a.batch, max_seq=a.seq)
+    dec = Decoder(plan, device=0)
     gen = torch.Generator(device=dev)
 
     def randn(shape, seed, std=0.02):
@@ -132,8 +142,8 @@ def case_step(a) -> str:
     dec.set_weight("lm_head.weight", randn((V, H), 12))
     ones = torch.ones(H, dtype=torch.float16, device=dev)
     dec.set_weight("model.norm.weight", ones)
-    shapes = {"self_attn.q_proj.weight": (4096, H), "self_attn.k_proj.weight": (1024, H),
-              "self_attn.v_proj.weight": (1024, H), "self_attn.o_proj.weight": (H, 4096),
+    shapes = {"self_attn.q_proj.weight": (Q * 128, H), "self_attn.k_proj.weight": (KV * 128, H),
+              "self_attn.v_proj.weight": (KV * 128, H), "self_attn.o_proj.weight": (H, Q * 128),
               "mlp.gate_proj.weight": (F, H), "mlp.up_proj.weight": (F, H),
               "mlp.down_proj.weight": (H, F)}
     for layer in range(a.layers):
@@ -152,8 +162,8 @@ def case_step(a) -> str:
     us = _timed(lambda: dec.step_device(tok, pos, ids), a.repeat)
     status = _native.device_status()
     dec.close()
-    return (f"step batch={a.batch} layers={a.layers} seq={a.seq}: {us / 1e3:.3f} ms/step, "
-            f"device status {status}")
+    return (f"step batch={a.batch} layers={a.layers} seq={a.seq} shard=1/{n}: "
+            f"{us / 1e3:.3f} ms/step, device status {status}")
 
 
 def main(argv=None) -> int:
@@ -188,6 +198,8 @@ def main(argv=None) -> int:
     s.add_argument("--layers", type=int, default=32)
     s.add_argument("--seq", type=int, default=4096)
     s.add_argument("--repeat", type=int, default=5)
+    s.add_argument("--shard", type=int, default=1, choices=[1, 2, 4, 8],
+                   help="one rank's share of tensor parallel over N GPUs, run alone")
     a = ap.parse_args(argv)
     cases = {"proj": case_proj, "flash": case_flash, "prefill": case_prefill, "step": case_step}
     print(cases[a.case](a), flush=True)

@@ -129,34 +129,22 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
   } else if (ep.kind == kEpiResid) {
     // Tensor parallel: all-reduce first.  The lead thread stores this rank's
     // partial as a tagged word, reads every rank's word for (b, n) over
-    // NVLink (all loads in flight at once, re-reading late ones) and adds
-    // them in rank order, as every rank does.
+    // NVLink (px_gather: all missing ranks' loads in flight together, round
+    // after round) and adds them in rank order, as every rank does.
     if (ep.px.seq >= 0 && lead) {
       const uint32_t tag = px_tag(ep.px, ep.px.seq);
 #pragma unroll
       for (int b = 0; b < BT; ++b)
         if (b < ep.batch) px_store(ep.px, tag, b, n, acc[b]);
-      uint64_t wv[BT][kMaxRanks];
-#pragma unroll
-      for (int b = 0; b < BT; ++b)
-#pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r)
-          wv[b][r] = (b < ep.batch && r < ep.px.ranks)
-                         ? ld_relaxed_sys(ep.px.part[r] + px_offset(ep.px, b, n))
-                         : 0;
 #pragma unroll
       for (int b = 0; b < BT; ++b) {
+        if (b >= ep.batch) continue;
+        uint32_t bits[kMaxRanks];
+        px_gather(ep.px.part, ep.px.ranks, px_offset(ep.px, b, n), tag, bits);
         float sum = 0.f;
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) {
-          if (b < ep.batch && r < ep.px.ranks) {
-            uint32_t bits = static_cast<uint32_t>(wv[b][r]);
-            if (static_cast<uint32_t>(wv[b][r] >> 32) != tag &&
-                !px_get(ep.px.part[r] + px_offset(ep.px, b, n), tag, &bits))
-              bits = 0;
-            sum += __uint_as_float(bits);
-          }
-        }
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < ep.px.ranks) sum += __uint_as_float(bits[r]);
         acc[b] = sum;
       }
     }

@@ -66,6 +66,33 @@ __device__ __forceinline__ bool px_get(const uint64_t* p, uint32_t tag, uint32_t
   return false;
 }
 
+// The word at offset `off` of every rank's buffer, once each carries `tag`:
+// every round issues the loads of all ranks still missing at once and checks
+// them together, so waiting for the slowest rank costs one NVLink round trip
+// per round rather than one per rank.  v[r] gets rank r's low 32 bits (0 where
+// a rank never arrived within the bound, which is reported).
+__device__ __forceinline__ bool px_gather(uint64_t* const* part, int ranks, size_t off, uint32_t tag,
+                                          uint32_t (&v)[kMaxRanks]) {
+  uint32_t missing = (1u << ranks) - 1u;
+#pragma unroll
+  for (int r = 0; r < kMaxRanks; ++r) v[r] = 0;
+  for (uint32_t i = 0; i < kMaxPolls && missing != 0; ++i) {
+    uint64_t w[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) w[r] = (missing >> r) & 1u ? ld_relaxed_sys(part[r] + off) : 0;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (((missing >> r) & 1u) && static_cast<uint32_t>(w[r] >> 32) == tag) {
+        v[r] = static_cast<uint32_t>(w[r]);
+        missing &= ~(1u << r);
+      }
+    }
+    if (missing != 0 && i >= 64) __nanosleep(32);
+  }
+  if (missing != 0) report_error(kDevErrPeerTimeout);
+  return missing == 0;
+}
+
 // Offset of (b, n) in a rank's partial buffer for exchange x.seq.
 __device__ __forceinline__ size_t px_offset(const PeerExchange& x, int b, int n) {
   return (static_cast<size_t>(x.seq & 1) * x.max_batch + b) * x.hidden + n;

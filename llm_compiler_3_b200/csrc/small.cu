@@ -57,24 +57,16 @@ __global__ void __launch_bounds__(kChunk)
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] +
         p.partial[static_cast<size_t>(b) * p.hidden + n];
   } else {
-    // Every rank's partial (tagged words: all loads in flight at once, then
-    // late ones re-read until they have landed), added in rank order: the
-    // same bits on every rank.
+    // Every rank's partial (tagged words gathered with all missing ranks'
+    // loads in flight together), added in rank order: the same bits on every
+    // rank.
     const uint32_t tag = px_tag(p.px, p.px.seq);
-    const size_t off = px_offset(p.px, b, n);
-    uint64_t w[kMaxRanks];
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) w[r] = r < p.px.ranks ? ld_relaxed_sys(p.px.part[r] + off) : 0;
+    uint32_t bits[kMaxRanks];
+    px_gather(p.px.part, p.px.ranks, px_offset(p.px, b, n), tag, bits);
     float sum = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-      if (r < p.px.ranks) {
-        uint32_t bits = static_cast<uint32_t>(w[r]);
-        if (static_cast<uint32_t>(w[r] >> 32) != tag && !px_get(p.px.part[r] + off, tag, &bits))
-          bits = 0;
-        sum += __uint_as_float(bits);
-      }
-    }
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < p.px.ranks) sum += __uint_as_float(bits[r]);
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] + sum;
   }
   const float w = __half2float(p.norm_w[n]);
@@ -189,14 +181,13 @@ __global__ void argmax_combine_peers_kernel(const PeerExchange px, int batch,
     const uint32_t tag = px_tag(px, kArgmaxSeq);
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    bool ok = true;
+    uint32_t vb[kMaxRanks], ib[kMaxRanks];
+    const size_t off = px_argmax_offset(px, b);
+    const bool ok = px_gather(px.part, px.ranks, off, tag, vb) &&
+                    px_gather(px.part, px.ranks, off + 1, tag, ib);
     for (int r = 0; r < px.ranks && ok; ++r) {
-      const uint64_t* w = px.part[r] + px_argmax_offset(px, b);
-      uint32_t vb = 0, ib = 0;
-      ok = px_get(w, tag, &vb) && px_get(w + 1, tag, &ib);
-      if (!ok) break;
-      const float v = __uint_as_float(vb);
-      const int i = static_cast<int>(ib);
+      const float v = __uint_as_float(vb[r]);
+      const int i = static_cast<int>(ib[r]);
       if (better(v, i, bv, bi)) {
         bv = v;
         bi = i;
