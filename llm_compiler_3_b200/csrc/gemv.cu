@@ -263,11 +263,14 @@ GemvLaunch choose_launch(int n_rows, int k) {
   long long best_score = -1;
   for (int per_sm = 1; per_sm <= 4; ++per_sm) {
     const long long avail = kGemvSmemPerSm / per_sm - kGemvSmemReserved - static_cast<long long>(fixed);
-    const int stages = static_cast<int>(std::min<long long>(kMaxStages, avail / kStageBytes));
+    int stages = static_cast<int>(std::min<long long>(kMaxStages, avail / kStageBytes));
     if (stages < 4) break;
     const int slots = per_sm * sms;
     const int rounds = (n_groups + slots - 1) / slots;
     const int grid = (n_groups + rounds - 1) / rounds;
+    // No deeper than the stages a CTA streams in all: shared memory it would
+    // not fill only keeps the next kernel's CTAs from becoming resident early.
+    stages = std::min(stages, std::max(4, rounds * kstages));
     const long long score =
         std::min<long long>(static_cast<long long>(grid) * stages * kStageBytes, 12ll << 20);
     if (score > best_score || (score == best_score && (grid > best.grid ||
