@@ -135,10 +135,13 @@ __device__ __forceinline__ void column_argmax(const float* tile_s, int first_row
   }
 }
 
-// Epilogue of one 16-token chunk of a finished 128-row tile.  Thread r holds
+// Epilogue of one 16-token chunk of a finished 128-row tile, for the
+// epilogue kind KIND (ep.kind): each instantiation of the kernel carries only
+// its own epilogue's code.  Thread r holds
 // row tile*128 + r for tokens b0 .. b0+15 in v[]; tokens at or past col_end
 // are skipped.  All branches depend only on the tile and the chunk, so every
 // epilogue thread reaches the same barriers.
+template <int KIND>
 __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile, int r, int b0,
                                                    float (&v)[kChunkCols], const float* rn,
                                                    float* tile_s, float* aux, const int* pos_s,
@@ -148,7 +151,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
 #pragma unroll
   for (int q = 0; q < kChunkCols; ++q) v[q] *= rn[b0 + q];
 
-  if (ep.kind == kEpiStore) {
+  if constexpr (KIND == kEpiStore) {
     const int n = tile * 128 + r;
     if (n < ep.n_rows) {
       const float bias = ep.bias ? __half2float(ep.bias[n]) : 0.f;
@@ -168,7 +171,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
         }
       }
     }
-  } else if (ep.kind == kEpiResid) {
+  } else if constexpr (KIND == kEpiResid) {
     const int n = tile * 128 + r;
     const bool valid = n < ep.n_rows;
     const float w = valid ? __half2float(ep.norm_w[n]) : 0.f;
@@ -213,7 +216,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
         ep.ssq_out[static_cast<size_t>(tile) * ep.ssq_out_ld + b0 + r] = aux[r];
     }
     epi_sync();
-  } else if (ep.kind == kEpiSwiGLU) {
+  } else if constexpr (KIND == kEpiSwiGLU) {
     // Rows come in (gate_j, up_j) pairs: even row r holds gate, r + 1 holds up,
     // j = tile * 64 + r / 2.  The partner is the neighbouring lane.
     const int j = tile * 64 + (r >> 1);
@@ -226,7 +229,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
             __float2half_rn(g / (1.f + expf(-g)) * u);
       }
     }
-  } else if (ep.kind == kEpiQKV) {
+  } else if constexpr (KIND == kEpiQKV) {
     // Head tiles store head dims in rotate_half pair order: row r holds dim
     // d = r / 2 + 64 * (r % 2), so RoPE partners (d, d + 64) are adjacent lanes.
     const bool is_q = tile < ep.q_heads;
@@ -288,7 +291,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
         }
       }
     }
-  } else if (ep.kind == kEpiArgmax) {
+  } else if constexpr (KIND == kEpiArgmax) {
     const int n = tile * 128 + r;
     const bool valid = n < ep.n_rows;
 #pragma unroll
@@ -330,7 +333,7 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
   }
 }
 
-template <int BN>
+template <int BN, int KIND>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ EpiParams ep, const uint8_t* __restrict__ w_packed,
@@ -571,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           float v[kChunkCols];
 #pragma unroll
           for (int q = 0; q < kChunkCols; ++q) v[q] = __uint_as_float(rr[q]);
-          run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
+          run_epilogue_chunk<KIND>(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
@@ -656,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
             for (int q = 0; q < kChunkCols; ++q) v[q] += t[q];
           }
-          run_epilogue_chunk(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
+          run_epilogue_chunk<KIND>(ep, tile, r, c0, v, rn, tile_s, aux, pos_s, ep.batch);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
@@ -719,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
               if (b0 + q < c_end) v[q] += src[q * 128];
             if (m != crank) ++j;
           }
-          run_epilogue_chunk(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
+          run_epilogue_chunk<KIND>(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
         }
         ok = false;  // done: the shared-memory pull below is for mode 1
       }
@@ -745,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
             for (int q = 0; q < kChunkCols; ++q) v[q] += t[u][q];
         }
-        run_epilogue_chunk(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
+        run_epilogue_chunk<KIND>(ep, tile, r, b0, v, rn, tile_s, aux, pos_s, c_end);
       }
     }
     if (clustered == 1) cluster_sync_all();  // no CTA leaves while a peer may still read its partial
@@ -887,13 +890,13 @@ Geometry geometry(int n_rows, int k, int batch) {
   return g;
 }
 
-template <int BN>
-int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& ep,
-                const uint8_t* w_packed, const Geometry& g, float* slots, uint32_t* counters,
-                cudaStream_t stream, bool pdl) {
+template <int BN, int KIND>
+int launch_proj_kind(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& ep,
+                     const uint8_t* w_packed, const Geometry& g, float* slots, uint32_t* counters,
+                     cudaStream_t stream, bool pdl) {
   const int stages = stages_for<BN>();
   const size_t smem = smem_for<BN>(stages);
-  auto kern = proj_kernel<BN>;
+  auto kern = proj_kernel<BN, KIND>;
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
   LaunchCfg cfg;
@@ -905,6 +908,26 @@ int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& e
   cfg.cluster = g.split > 1 ? g.split : 1;
   return launch(cfg, kern, wm, xm, ep, w_packed, g.n_tiles, g.kblocks, stages, g.mode, slots,
                 counters);
+}
+
+template <int BN>
+int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& ep,
+                const uint8_t* w_packed, const Geometry& g, float* slots, uint32_t* counters,
+                cudaStream_t stream, bool pdl) {
+  switch (ep.kind) {
+    case kEpiStore:
+      return launch_proj_kind<BN, kEpiStore>(wm, xm, ep, w_packed, g, slots, counters, stream, pdl);
+    case kEpiResid:
+      return launch_proj_kind<BN, kEpiResid>(wm, xm, ep, w_packed, g, slots, counters, stream, pdl);
+    case kEpiSwiGLU:
+      return launch_proj_kind<BN, kEpiSwiGLU>(wm, xm, ep, w_packed, g, slots, counters, stream,
+                                              pdl);
+    case kEpiQKV:
+      return launch_proj_kind<BN, kEpiQKV>(wm, xm, ep, w_packed, g, slots, counters, stream, pdl);
+    default:
+      return launch_proj_kind<BN, kEpiArgmax>(wm, xm, ep, w_packed, g, slots, counters, stream,
+                                              pdl);
+  }
 }
 
 // One thread per 16-byte chunk of the source: row i, chunk c (elements 8c..8c+7)

@@ -73,7 +73,9 @@ def test_ragged_and_empty_sequences(cuda):
 
 
 @pytest.mark.parametrize("batch,kv,dim,lens", [(1, 1, 128, [4096]), (2, 2, 128, [700, 0]),
-                                                (1, 4, 64, [333]), (4, 1, 128, [1, 31, 32, 1000])])
+                                                (1, 4, 64, [333]), (4, 1, 128, [1, 31, 32, 1000]),
+                                                (2, 2, 64, [4096, 2500]),
+                                                (4, 1, 128, [3000, 0, 4096, 17])])
 def test_small_batch_cluster_merge(cuda, batch, kv, dim, lens):
     """At most 4 (sequence, KV head) units with automatic splits: the splits of
     a unit run as one thread-block cluster and merge through distributed shared
