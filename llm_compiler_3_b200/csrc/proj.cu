@@ -141,6 +141,12 @@ __device__ __forceinline__ void column_argmax(const float* tile_s, int first_row
 // row tile*128 + r for tokens b0 .. b0+15 in v[]; tokens at or past col_end
 // are skipped.  All branches depend only on the tile and the chunk, so every
 // epilogue thread reaches the same barriers.
+// A STORE whose values go to this rank's peer-exchange buffer as tagged
+// words (px.seq >= 0) is instantiated apart from the plain STORE: the
+// exchange's system-scope store in the plain STORE's loop, even untaken, made
+// every chunk ~1500 cycles slower.
+constexpr int kEpiStorePeer = 16;
+
 template <int KIND>
 __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile, int r, int b0,
                                                    float (&v)[kChunkCols], const float* rn,
@@ -162,12 +168,25 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
           float val = v[q] + bias;
           if (ep.relu) val = fmaxf(val, 0.f);
           const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
-          if (ep.px.seq >= 0)
-            px_store(ep.px, px_tag(ep.px, ep.px.seq), b, n, val);
-          else if (ep.out_f32)
+          if (ep.out_f32)
             static_cast<float*>(ep.out)[off] = val;
           else
             static_cast<__half*>(ep.out)[off] = __float2half_rn(val);
+        }
+      }
+    }
+  } else if constexpr (KIND == kEpiStorePeer) {
+    const int n = tile * 128 + r;
+    if (n < ep.n_rows) {
+      const float bias = ep.bias ? __half2float(ep.bias[n]) : 0.f;
+      const uint32_t tag = px_tag(ep.px, ep.px.seq);
+#pragma unroll
+      for (int q = 0; q < kChunkCols; ++q) {
+        const int b = b0 + q;
+        if (b < batch) {
+          float val = v[q] + bias;
+          if (ep.relu) val = fmaxf(val, 0.f);
+          px_store(ep.px, tag, b, n, val);
         }
       }
     }
@@ -277,19 +296,21 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
     } else {
       const int kh = is_k ? tile - ep.q_heads : tile - ep.q_heads - ep.kv_heads;
       __half* cache = is_k ? ep.k_cache : ep.v_cache;
+      bool out_of_cache = false;  // reported once, after the loop (an atomic in it slows it)
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q) {
         const int b = b0 + q;
         if (b < batch) {
           const int pos = pos_s[b];
           if (pos < 0 || pos >= ep.max_seq) {
-            if (r == 0) report_error(kDevErrBounds);
+            out_of_cache = true;
           } else {
             cache[static_cast<size_t>(b) * ep.cache_batch_stride +
                   (static_cast<size_t>(kh) * ep.max_seq + pos) * 128 + d] = __float2half_rn(v[q]);
           }
         }
       }
+      if (out_of_cache && r == 0) report_error(kDevErrBounds);
     }
   } else if constexpr (KIND == kEpiArgmax) {
     const int n = tile * 128 + r;
@@ -916,6 +937,9 @@ int launch_proj(const CUtensorMap& wm, const CUtensorMap& xm, const EpiParams& e
                 cudaStream_t stream, bool pdl) {
   switch (ep.kind) {
     case kEpiStore:
+      if (ep.px.seq >= 0)
+        return launch_proj_kind<BN, kEpiStorePeer>(wm, xm, ep, w_packed, g, slots, counters, stream,
+                                                   pdl);
       return launch_proj_kind<BN, kEpiStore>(wm, xm, ep, w_packed, g, slots, counters, stream, pdl);
     case kEpiResid:
       return launch_proj_kind<BN, kEpiResid>(wm, xm, ep, w_packed, g, slots, counters, stream, pdl);
