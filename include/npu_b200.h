@@ -118,8 +118,8 @@ NPU_B200_API int npu_b200_flash_decode(const void* d_q, const void* d_k, const v
  * last uncaptured call on that device found, so make the first call on each
  * device before any stream capture (also after cudaDeviceReset, which reloads
  * the module).  Every call uses the same array and clears the split counters it
- * needs before its kernel runs; shapes whose splits merge inside one thread-block
- * cluster (at most 4 sequence x KV-head units, num_splits 0) touch no scratch.
+ * needs before its kernel runs; a call with one split per unit touches no
+ * scratch.
  * Calls that overlap on the GPU (different streams, or concurrent graphs) race
  * on the array.  Arguments and results are those of npu_b200_flash_decode. */
 NPU_B200_API int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, const void* d_v,

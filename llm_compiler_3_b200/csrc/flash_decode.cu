@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                         const int32_t* __restrict__ seq_lens, __half* __restrict__ out,
                         float* __restrict__ part, uint32_t* __restrict__ counters, int q_heads,
                         int kv_heads, int max_seq, int keys_per_split, int num_splits,
-                        float scale_log2, const int32_t* __restrict__ positions, int clustered) {
+                        float scale_log2, const int32_t* __restrict__ positions) {
   using S = FdShape<D>;
   constexpr int KSTEPS = D / 16;  // k-steps of the score MMA
   constexpr int DBLK = D / 16;    // 16-dim blocks of the PV MMA
@@ -307,160 +307,161 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   __syncthreads();
 
   const size_t unit = static_cast<size_t>(b) * kv_heads + h;
-  // Clustered (small batch): the splits of one (sequence, KV head) are one
-  // thread-block cluster; each keeps its partial in its own shared memory and
-  // member 0 merges them through distributed shared memory.
-  float* cp_o = co + WARPS * kMaxGroup * D;  // [8][D] this CTA's O
-  float* cp_m = cp_o + kMaxGroup * D;        // [8] max (log2 domain)
-  float* cp_l = cp_m + kMaxGroup;            // [8] row sums
-  float* my_part = clustered ? nullptr : part + (unit * num_splits + split) * S::kPartFloats;
-  for (int idx = threadIdx.x; idx < group * D; idx += WARPS * 32) {
-    const int head = idx / D, dim = idx - head * D;
+  // Split partials of one unit are contiguous, `pitch` floats each: O
+  // [group][D], m [group] (log2 domain), l [group], padded to 16 bytes (at
+  // most kPartFloats).
+  const int pitch = (group * D + 2 * group + 3) & ~3;
+  float* my_part = part + (unit * num_splits + split) * pitch;
+  // The warps' weights exp2(m_w - m) per head, the CTA's max m and row sum,
+  // formed once per head; then each thread combines one 4-dim slice.
+  float* cw = co + WARPS * kMaxGroup * D;  // [WARPS][8]
+  float* cM = cw + WARPS * kMaxGroup;  // [8]
+  float* cL = cM + kMaxGroup;          // [8]
+  if (threadIdx.x < group) {
+    const int head = threadIdx.x;
     float mx = -INFINITY;
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) mx = fmaxf(mx, cm[w * kMaxGroup + head]);
-    float L = 0.f, O = 0.f;
+    float L = 0.f;
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) {
       const float mw = cm[w * kMaxGroup + head];
       const float wt = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+      cw[w * kMaxGroup + head] = wt;
       L += cl[w * kMaxGroup + head] * wt;
-      O += co[(w * kMaxGroup + head) * D + dim] * wt;
+    }
+    cM[head] = mx;
+    cL[head] = L;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < group * D / 4; idx += WARPS * 32) {
+    const int head = (idx * 4) / D, dim = idx * 4 - head * D;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+      const float wt = cw[w * kMaxGroup + head];
+      const float4 v = *reinterpret_cast<const float4*>(co + (w * kMaxGroup + head) * D + dim);
+      O.x += v.x * wt;
+      O.y += v.y * wt;
+      O.z += v.z * wt;
+      O.w += v.w * wt;
     }
     if (num_splits == 1) {
-      out[(static_cast<size_t>(b) * q_heads + h * group + head) * D + dim] =
-          __float2half_rn(L > 0.f ? O / L : 0.f);
-    } else if (clustered) {
-      cp_o[head * D + dim] = O;
-      if (dim == 0) {
-        cp_m[head] = mx;
-        cp_l[head] = L;
-      }
+      const float L = cL[head];
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      __half2* dst = reinterpret_cast<__half2*>(
+          out + (static_cast<size_t>(b) * q_heads + h * group + head) * D + dim);
+      dst[0] = __floats2half2_rn(O.x * inv, O.y * inv);
+      dst[1] = __floats2half2_rn(O.z * inv, O.w * inv);
     } else {
-      my_part[head * D + dim] = O;
+      *reinterpret_cast<float4*>(my_part + head * D + dim) = O;
       if (dim == 0) {
-        my_part[kMaxGroup * D + head] = mx;
-        my_part[kMaxGroup * D + kMaxGroup + head] = L;
+        my_part[group * D + head] = cM[head];
+        my_part[group * D + group + head] = cL[head];
       }
     }
   }
   if (num_splits == 1) return;
 
-  if (clustered) {
-    cluster_sync_all();  // every member's partial is in its shared memory
-    if (split == 0) {
-      for (int idx = threadIdx.x; idx < group * D; idx += WARPS * 32) {
-        const int head = idx / D, dim = idx - head * D;
-        float mr[8], lr[8], orr[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          if (r < num_splits) {
-            mr[r] = ld_cluster_f32(cluster_map(smem_u32(cp_m + head), r));
-            lr[r] = ld_cluster_f32(cluster_map(smem_u32(cp_l + head), r));
-            orr[r] = ld_cluster_f32(cluster_map(smem_u32(cp_o + head * D + dim), r));
-          } else {
-            mr[r] = -INFINITY;
-            lr[r] = orr[r] = 0.f;
-          }
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) mx = fmaxf(mx, mr[r]);
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const float wt = mr[r] == -INFINITY ? 0.f : fast_exp2(mr[r] - mx);
-          L += lr[r] * wt;
-          O += orr[r] * wt;
-        }
-        out[(static_cast<size_t>(b) * q_heads + h * group + head) * D + dim] =
-            __float2half_rn(L > 0.f ? O / L : 0.f);
-      }
-    }
-    cluster_sync_all();  // no member leaves while member 0 reads its shared memory
-    return;
-  }
-
-  // Last CTA of this (sequence, KV head) merges every split.
-  __threadfence();
+  // Last CTA of this (sequence, KV head) merges every split.  One thread
+  // releases the CTA's partial (ordered before it by the barrier) with its
+  // count; the CTA that completes the count acquires the others'.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const uint32_t prev = atomicAdd(&counters[unit], 1u);
     s_last = (prev == static_cast<uint32_t>(num_splits - 1)) ? 1 : 0;
+    if (s_last) __threadfence();
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
-  // Merge without serial L2 round trips.  The splits' outputs (group x D
-  // floats each) come into the idle stage buffers with one bulk copy per split
-  // when they fit, all in flight together; the statistics are fetched at
-  // once; one warp per head forms the split weights with lane-parallel
-  // reductions; then each thread sums one 4-dim slice over the splits.
-  const float* up = part + unit * num_splits * S::kPartFloats;
-  const int slab = group * D;  // floats of one split's outputs
-  const bool staged = static_cast<size_t>(num_splits) * slab * 4 + 2 * num_splits * kMaxGroup * 4 +
-                          64 <= static_cast<size_t>(WARPS) * STAGES * S::kStageBytes;
-  float* po = reinterpret_cast<float*>(smem);                   // [num_splits][slab] if staged
-  float* sw = staged ? po + num_splits * slab : po;             // [num_splits][8] m, then weights
-  float* sl = sw + num_splits * kMaxGroup;                      // [num_splits][8] l
-  float* sL = sl + num_splits * kMaxGroup;                      // [8] merged row sums
-  if (staged && threadIdx.x == 0) {
-    // The partials were written by other CTAs' generic stores, and the stage
-    // buffers were last used by this CTA's generic accesses: order both before
-    // this thread's bulk (async-proxy) copies.
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(merge_bar, static_cast<uint32_t>(num_splits * slab * 4));
-    const uint64_t pol = policy_evict_first();
-    for (int sp = 0; sp < num_splits; ++sp)
-      bulk_load_hint(po + sp * slab, up + sp * S::kPartFloats, slab * 4, merge_bar, pol);
+  // Merge with one L2 round trip: the unit's partials (contiguous) come into
+  // the idle stage buffers with one bulk copy when they fit (else they are read
+  // from L2 directly); one warp per head forms the split weights with
+  // lane-parallel reductions; then each thread sums one 4-dim slice over the
+  // splits.
+  const float* up = part + unit * num_splits * pitch;
+  const int slab = group * D;  // floats of one split's outputs; m and l follow
+  const uint32_t unit_bytes = static_cast<uint32_t>(num_splits) * pitch * 4u;
+  const bool staged = unit_bytes + 2 * static_cast<size_t>(num_splits) * kMaxGroup * 4 + 64 <=
+                      static_cast<size_t>(WARPS) * STAGES * S::kStageBytes;
+  const float* src = staged ? reinterpret_cast<const float*>(smem) : up;
+  float* sw = reinterpret_cast<float*>(smem) + (staged ? num_splits * pitch : 0);  // [splits][8] weights
+  float* sL = sw + num_splits * kMaxGroup;  // [8] merged row sums
+  bool ready = true;
+  if (staged) {
+    if (threadIdx.x == 0) {
+      // The partials were written by other CTAs' generic stores, and the stage
+      // buffers were last used by this CTA's generic accesses: order both
+      // before this thread's bulk (async-proxy) copy.
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(merge_bar, unit_bytes);
+      bulk_load_hint(smem, up, unit_bytes, merge_bar, policy_evict_first());
+    }
+    ready = mbar_wait(merge_bar, 0, kDevErrTmaTimeout);
   }
-  for (int i = threadIdx.x; i < num_splits * group; i += WARPS * 32) {
-    const int sp = i / group, head = i - sp * group;
-    const float* ps = up + sp * S::kPartFloats + kMaxGroup * D;
-    sw[sp * kMaxGroup + head] = __ldcg(ps + head);
-    sl[sp * kMaxGroup + head] = __ldcg(ps + kMaxGroup + head);
-  }
-  __syncthreads();
-  for (int head = warp; head < group; head += WARPS) {
+  // Split statistics: m at slab + head, l at slab + group + head of each split.
+  auto stat = [&](int sp, int at) {
+    const float* ps = src + static_cast<size_t>(sp) * pitch + slab + at;
+    return staged ? *ps : __ldcg(ps);
+  };
+  for (int head = warp; ready && head < group; head += WARPS) {
     float mx = -INFINITY;
-    for (int sp = lane; sp < num_splits; sp += 32) mx = fmaxf(mx, sw[sp * kMaxGroup + head]);
+    for (int sp = lane; sp < num_splits; sp += 32) mx = fmaxf(mx, stat(sp, head));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float L = 0.f;
     for (int sp = lane; sp < num_splits; sp += 32) {
-      const float ms = sw[sp * kMaxGroup + head];
+      const float ms = stat(sp, head);
       const float wt = ms == -INFINITY ? 0.f : fast_exp2(ms - mx);
       sw[sp * kMaxGroup + head] = wt;
-      L += sl[sp * kMaxGroup + head] * wt;
+      L += stat(sp, group + head) * wt;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     if (lane == 0) sL[head] = L;
   }
   __syncthreads();
-  bool ready = true;
-  if (staged) ready = mbar_wait(merge_bar, 0, kDevErrTmaTimeout);
   for (int idx = threadIdx.x; ready && idx < group * D / 4; idx += WARPS * 32) {
     const int head = (idx * 4) / D, dim = idx * 4 - head * D;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int sp = 0; sp < num_splits; ++sp) {
-      const float wt = sw[sp * kMaxGroup + head];
-      const float4 pv =
-          staged ? *reinterpret_cast<const float4*>(po + sp * slab + head * D + dim)
-                 : __ldcg(reinterpret_cast<const float4*>(up + sp * S::kPartFloats + head * D + dim));
-      acc.x += wt * pv.x;
-      acc.y += wt * pv.y;
-      acc.z += wt * pv.z;
-      acc.w += wt * pv.w;
+    const float* col = src + head * D + dim;
+    const float* wcol = sw + head;
+    // Two independent chains (even and odd splits), added at the end.
+    auto part_at = [&](int sp) {
+      const float4* at = reinterpret_cast<const float4*>(col + static_cast<size_t>(sp) * pitch);
+      return staged ? *at : __ldcg(at);
+    };
+    float4 e = make_float4(0.f, 0.f, 0.f, 0.f), o = e;
+    int sp = 0;
+#pragma unroll 4
+    for (; sp + 1 < num_splits; sp += 2) {
+      const float w0 = wcol[sp * kMaxGroup], w1 = wcol[(sp + 1) * kMaxGroup];
+      const float4 p0 = part_at(sp), p1 = part_at(sp + 1);
+      e.x += w0 * p0.x;
+      e.y += w0 * p0.y;
+      e.z += w0 * p0.z;
+      e.w += w0 * p0.w;
+      o.x += w1 * p1.x;
+      o.y += w1 * p1.y;
+      o.z += w1 * p1.z;
+      o.w += w1 * p1.w;
     }
+    if (sp < num_splits) {
+      const float w0 = wcol[sp * kMaxGroup];
+      const float4 p0 = part_at(sp);
+      e.x += w0 * p0.x;
+      e.y += w0 * p0.y;
+      e.z += w0 * p0.z;
+      e.w += w0 * p0.w;
+    }
+    const float4 o4 = make_float4(e.x + o.x, e.y + o.y, e.z + o.z, e.w + o.w);
     const float L = sL[head];
     const float inv = L > 0.f ? 1.f / L : 0.f;
     __half2* dst = reinterpret_cast<__half2*>(
         out + (static_cast<size_t>(b) * q_heads + h * group + head) * D + dim);
-    dst[0] = __floats2half2_rn(acc.x * inv, acc.y * inv);
-    dst[1] = __floats2half2_rn(acc.z * inv, acc.w * inv);
+    dst[0] = __floats2half2_rn(o4.x * inv, o4.y * inv);
+    dst[1] = __floats2half2_rn(o4.z * inv, o4.w * inv);
   }
   if (threadIdx.x == 0) counters[unit] = 0u;  // leave the workspace reusable
 }
@@ -474,8 +475,10 @@ constexpr size_t fd_smem_bytes() {
          (kWarps * kStages + 1) * sizeof(uint64_t);
 }
 
-// Splits per (sequence, KV head): the count whose waves of CTAs finish first,
-// charging each CTA a fixed start-up cost equivalent to ~96 keys.
+// Splits per (sequence, KV head): the count whose waves of CTAs (one per SM)
+// finish first, charging each CTA a fixed start-up cost equivalent to ~96 keys
+// and each split ~6 keys of the merge (measured on 1-8 units of 4096 keys:
+// 32 splits for 1-2 units, 16 for 8).
 int choose_splits(int units, int max_seq, int sms) {
   int best = 1;
   double best_cost = 1e300;
@@ -486,7 +489,7 @@ int choose_splits(int units, int max_seq, int sms) {
     if (s_eff != s) continue;
     const long ctas = static_cast<long>(units) * s_eff;
     const long waves = (ctas + sms - 1) / sms;
-    const double cost = static_cast<double>(waves) * (kps + 96);
+    const double cost = static_cast<double>(waves) * (kps + 96) + 6.0 * s_eff;
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = s_eff;
@@ -505,28 +508,15 @@ int resolve_splits(int batch, int kv_heads, int max_seq, int num_splits, int* kp
   return s;
 }
 
-// The launch shape of one call: key splits per (sequence, KV head), keys per
-// split, and whether the splits of a unit run as one cluster merging through
-// distributed shared memory (then no workspace is used at all).  At most 4
-// units (batch-1 decode of a tensor-parallel shard; the split count left to
-// us): 8 splits per unit as one cluster -- no workspace, no second round trip
-// through L2.  With more units the cluster launch's wait for 8 free SMs of one
-// GPC behind the previous kernel costs more than it saves.
+// The launch shape of one call: key splits per (sequence, KV head) and keys
+// per split.
 struct FdLaunch {
   int splits = 1, kps = 0;
-  bool clustered = false;
 };
 
 FdLaunch plan_fd(int batch, int kv_heads, int max_seq, int num_splits) {
   FdLaunch L;
   L.splits = resolve_splits(batch, kv_heads, max_seq, num_splits, &L.kps);
-  if (num_splits == 0 && static_cast<long long>(batch) * kv_heads <= 4 && max_seq > kKeysPerTile) {
-    int kps = (max_seq + 7) / 8;
-    kps = (kps + kKeysPerTile - 1) / kKeysPerTile * kKeysPerTile;
-    L.kps = kps;
-    L.splits = (max_seq + kps - 1) / kps;
-    L.clustered = L.splits > 1;
-  }
   return L;
 }
 
@@ -542,7 +532,7 @@ template <int D>
 int launch_fd(const CUtensorMap& km, const CUtensorMap& vm, const __half* q, const int32_t* lens,
               __half* out, float* part, uint32_t* counters, int batch, int q_heads, int kv_heads,
               int max_seq, int kps, int splits, float scale_log2, cudaStream_t stream, bool pdl,
-              const int32_t* positions, bool clustered) {
+              const int32_t* positions) {
   auto kern = flash_decode_kernel<D, kWarps, kStages>;
   constexpr size_t smem = fd_smem_bytes<D>();
   NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -553,9 +543,8 @@ int launch_fd(const CUtensorMap& km, const CUtensorMap& vm, const __half* q, con
   cfg.smem = smem;
   cfg.stream = stream;
   cfg.pdl = pdl;
-  cfg.cluster = clustered ? splits : 1;
   return launch(cfg, kern, km, vm, q, lens, out, part, counters, q_heads, kv_heads, max_seq, kps,
-                splits, scale_log2, positions, clustered ? 1 : 0);
+                splits, scale_log2, positions);
 }
 
 }  // namespace
@@ -588,8 +577,7 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
               num_splits, kMaxSplits);
   const FdLaunch L = plan_fd(batch, kv_heads, max_seq, num_splits);
   const int kps = L.kps, splits = L.splits;
-  const bool clustered = L.clustered;
-  const size_t need = clustered ? 0 : workspace_bytes_for(batch, kv_heads, head_dim, splits);
+  const size_t need = workspace_bytes_for(batch, kv_heads, head_dim, splits);
   NPU_REQUIRE(need == 0 || (workspace && workspace_bytes >= need),
               "flash_decode: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   NPU_REQUIRE(need == 0 || (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
@@ -611,15 +599,15 @@ int flash_decode_run(const void* q, const void* k, const void* v, const int32_t*
   __half* oh = static_cast<__half*>(out);
   if (head_dim == 128)
     return launch_fd<128>(km, vm, qh, seq_lens, oh, part, counters, batch, q_heads, kv_heads,
-                          max_seq, kps, splits, scale_log2, stream, pdl, positions, clustered);
+                          max_seq, kps, splits, scale_log2, stream, pdl, positions);
   return launch_fd<64>(km, vm, qh, seq_lens, oh, part, counters, batch, q_heads, kv_heads,
-                       max_seq, kps, splits, scale_log2, stream, pdl, positions, clustered);
+                       max_seq, kps, splits, scale_log2, stream, pdl, positions);
 }
 
 size_t flash_decode_workspace(int batch, int kv_heads, int head_dim, int max_seq, int num_splits) {
   if (batch < 1 || kv_heads < 1 || max_seq < 1) return 0;
   const FdLaunch L = plan_fd(batch, kv_heads, max_seq, num_splits);
-  return L.clustered ? 0 : workspace_bytes_for(batch, kv_heads, head_dim, L.splits);
+  return workspace_bytes_for(batch, kv_heads, head_dim, L.splits);
 }
 
 }  // namespace npu_b200
@@ -635,9 +623,13 @@ extern "C" int npu_b200_flash_decode(const void* d_q, const void* d_k, const voi
                                      float scale, int num_splits, void* d_workspace,
                                      size_t workspace_bytes, void* stream) {
   npu_b200::clear_error();
+  // Launched as a programmatic dependent of the stream's previous work: the
+  // kernel reads no input and writes no output before griddepcontrol.wait
+  // (which returns once that work has completed), so only the launch and the
+  // barrier set-up overlap its tail.
   return npu_b200::flash_decode_run(d_q, d_k, d_v, d_seq_lens, d_out, batch, q_heads, kv_heads,
                                     head_dim, max_seq, scale, num_splits, d_workspace,
-                                    workspace_bytes, static_cast<cudaStream_t>(stream), false,
+                                    workspace_bytes, static_cast<cudaStream_t>(stream), true,
                                     nullptr);
 }
 
@@ -703,13 +695,13 @@ extern "C" int npu_b200_flash_decode_noalloc(const void* d_q, const void* d_k, c
   void* scratch = nullptr;
   int rc = scratch_address(s, &scratch);
   if (rc) return rc;
-  if (need > 0) {  // clustered launches merge in shared memory and use no scratch
+  if (need > 0) {  // a single split per unit merges nothing and uses no scratch
     // The array keeps whatever the previous call left: the split counters
     // must start at zero.
     const size_t units = static_cast<size_t>(batch) * kv_heads;
     NPU_TRY_CUDA(cudaMemsetAsync(scratch, 0, units * sizeof(uint32_t), s));
   }
   return flash_decode_run(d_q, d_k, d_v, d_seq_lens, d_out, batch, q_heads, kv_heads, head_dim,
-                          max_seq, scale, num_splits, scratch, kNoAllocScratchBytes, s, false,
+                          max_seq, scale, num_splits, scratch, kNoAllocScratchBytes, s, true,
                           nullptr);
 }

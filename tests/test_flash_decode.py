@@ -76,10 +76,10 @@ def test_ragged_and_empty_sequences(cuda):
                                                 (1, 4, 64, [333]), (4, 1, 128, [1, 31, 32, 1000]),
                                                 (2, 2, 64, [4096, 2500]),
                                                 (4, 1, 128, [3000, 0, 4096, 17])])
-def test_small_batch_cluster_merge(cuda, batch, kv, dim, lens):
-    """At most 4 (sequence, KV head) units with automatic splits: the splits of
-    a unit run as one thread-block cluster and merge through distributed shared
-    memory (ragged and empty sequences, garbage past each length)."""
+def test_small_batch_many_splits(cuda, batch, kv, dim, lens):
+    """At most 4 (sequence, KV head) units with automatic splits: 16-64 splits
+    per unit, merged by the unit's last CTA from one bulk copy of the unit's
+    partials (ragged and empty sequences, garbage past each length)."""
     group = 4
     max_seq = max(max(lens), 64)
     q = seeded((batch, kv * group, dim), 40 + batch)
