@@ -292,8 +292,12 @@ int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams
   const int kx = g.split > 1 ? std::min(k, (kstages + g.split - 1) / g.split * kPanelsPerStage * 64) : k;
   const size_t smem = gemv_smem<BT>(kx, g.stages);
   auto kern = gemv_kernel<BT>;
-  NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem)));
+  // The limit is the function's, shared by the launches of every shape (and
+  // by graph nodes a profiler relaunches after the capture): set it to the
+  // most any launch may use, never to this launch's size.
+  constexpr int kSmemLimit = kGemvSmemPerSm - kGemvSmemReserved;
+  NPU_REQUIRE(smem <= static_cast<size_t>(kSmemLimit), "gemv: %zu bytes of shared memory", smem);
+  NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
   if (g.split > 1)
     NPU_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   LaunchCfg cfg;

@@ -13,7 +13,16 @@
 // Buffer of each rank (zeroed once), uint64 words:
 //   [2][max_batch][hidden] partials, double-buffered by the parity of the
 //   exchange index (a rank can be at most one exchange ahead of a peer still
-//   reading), then [max_batch][2] (value, index) of the rank's LM-head argmax.
+//   reading), then [max_batch][2] (value, index) of the rank's LM-head argmax,
+//   then [2][max_batch][hidden] reduced sums of the rows this rank owns in a
+//   two-shot exchange (same parity rule).
+//
+// One-shot (batch 1-2, and whenever the volume is small): every rank reads
+// every rank's partials.  Two-shot (large batches over 3+ ranks): rank r owns
+// rows [r H/R, (r+1) H/R); it reads every rank's partials of those rows only,
+// adds them in rank order and publishes the sums; the other ranks read them
+// from it.  Each rank then takes 2 (R-1)/R of the data over NVLink instead of
+// R-1 times it, and every row is still added in rank order by one rank.
 // tag = 0x80000000 | (epoch * 256 + seq): epoch counts steps on every rank
 // alike, seq numbers the exchanges of a step, so a tag never repeats within
 // 2^23 steps and is never 0 (the zeroed buffer).
@@ -110,6 +119,12 @@ __device__ __forceinline__ bool px_load(const PeerExchange& x, uint32_t tag, int
   const bool ok = px_get(x.part[src] + px_offset(x, b, n), tag, &bits);
   *v = ok ? __uint_as_float(bits) : 0.f;
   return ok;
+}
+
+// Offset of (b, n)'s reduced sum (two-shot) in its owner's buffer.
+__device__ __forceinline__ size_t px_reduced_offset(const PeerExchange& x, int b, int n) {
+  return static_cast<size_t>(2) * x.max_batch * x.hidden + static_cast<size_t>(2) * x.max_batch +
+         (static_cast<size_t>(x.seq & 1) * x.max_batch + b) * x.hidden + n;
 }
 
 // Argmax words of a rank's buffer: (value, index) of token b.

@@ -361,7 +361,7 @@ int setup_peer_exchange(npu_b200_ctx* c) {
   const int T = c->tp_size;
   NPU_REQUIRE(T <= kMaxRanks, "tensor parallel: at most %d ranks", kMaxRanks);
   const size_t B = static_cast<size_t>(P.max_batch), H = static_cast<size_t>(P.hidden);
-  const size_t part_words = 2 * B * H + B * 2;
+  const size_t part_words = 4 * B * H + B * 2;  // partials, argmax, reduced sums (peer.cuh)
   int rc = 0;
   if ((rc = dalloc(c, part_words, &c->px_part))) return rc;
   const char* env = getenv("NPU_B200_TP_EXCHANGE");
@@ -769,6 +769,15 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
   if (c->px_ready) {
     u.px = c->px;
     u.px.seq = seq;
+    // Two-shot when the bytes it saves on each rank's NVLink, (R-1)(R-2)/R of
+    // the tagged partials, clearly outweigh its second hop and wait (taken as
+    // 4 MB, ~5 us at 770 GB/s): at batch 64 over 8 ranks it saves 11 MB
+    // (~14 us) per exchange; over 4 ranks 3 MB, where one hop less counts as
+    // much.
+    const int R = c->tp_size;
+    const double saved = static_cast<double>(R - 1) * (R - 2) / R * batch * P.hidden * 8.0;
+    u.two_shot = R >= 3 && P.hidden % (32 * R) == 0 && saved > 4e6 &&
+                 static_cast<long long>(P.hidden / 128) * batch <= 16ll * sm_count();
   }
   u.mode = kResidAddPartial;
   u.batch = batch;

@@ -59,14 +59,25 @@ __global__ void __launch_bounds__(kChunk)
   } else {
     // Every rank's partial (tagged words gathered with all missing ranks'
     // loads in flight together), added in rank order: the same bits on every
-    // rank.
+    // rank.  Two-shot: only for the rows this rank owns, whose sums it then
+    // publishes; other rows' sums come from their owners (a warp's 32 rows
+    // have one owner).
     const uint32_t tag = px_tag(p.px, p.px.seq);
-    uint32_t bits[kMaxRanks];
-    px_gather(p.px.part, p.px.ranks, px_offset(p.px, b, n), tag, bits);
+    const int owner = p.two_shot ? n / (p.hidden / p.px.ranks) : p.px.rank;
     float sum = 0.f;
+    if (owner == p.px.rank) {
+      uint32_t bits[kMaxRanks];
+      px_gather(p.px.part, p.px.ranks, px_offset(p.px, b, n), tag, bits);
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r)
-      if (r < p.px.ranks) sum += __uint_as_float(bits[r]);
+      for (int r = 0; r < kMaxRanks; ++r)
+        if (r < p.px.ranks) sum += __uint_as_float(bits[r]);
+      if (p.two_shot)
+        px_put(p.px.part[p.px.rank] + px_reduced_offset(p.px, b, n), tag, __float_as_uint(sum));
+    } else {
+      uint32_t bits = 0;
+      px_get(p.px.part[owner] + px_reduced_offset(p.px, b, n), tag, &bits);
+      sum = __uint_as_float(bits);
+    }
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] + sum;
   }
   const float w = __half2float(p.norm_w[n]);
@@ -232,6 +243,14 @@ __global__ void store_hidden_kernel(const float* __restrict__ resid, __half* __r
 int residual_update(const ResidualUpdate& p, cudaStream_t stream, bool pdl) {
   NPU_REQUIRE(p.hidden % kChunk == 0 && p.batch >= 1 && p.batch <= 1024,
               "residual update: hidden %d must be a multiple of 128", p.hidden);
+  // Two-shot: every rank's slice of rows a whole number of warps, and every
+  // CTA of the grid resident at once (128-thread CTAs, 16 per SM), so the
+  // CTAs that reduce this rank's rows get an SM while the others poll.
+  NPU_REQUIRE(!p.two_shot || (p.px.seq >= 0 && p.px.ranks >= 2 &&
+                              p.hidden % (p.px.ranks * 32) == 0 &&
+                              static_cast<long long>(p.hidden / kChunk) * p.batch <= 16ll * sm_count()),
+              "residual update: two-shot exchange needs hidden %% (32 x ranks) == 0 and a "
+              "co-resident grid");
   LaunchCfg cfg;
   cfg.grid = dim3(p.hidden / kChunk, p.batch);
   cfg.block = dim3(kChunk);

@@ -37,6 +37,7 @@ struct ResidualUpdate {
   float* rope_tab = nullptr;          // [batch][64] (cos, sin) of positions[b] * inv_freq[i]
   uint32_t* epoch = nullptr;          // optional: step counter to advance (first kernel of a step)
   PeerExchange px;                    // kResidAddPartial with px.seq >= 0: the ranks' partials
+  int two_shot = 0;                   // with px: reduce-scatter + all-gather (peer.cuh)
 };
 
 int residual_update(const ResidualUpdate& p, cudaStream_t stream, bool pdl);
