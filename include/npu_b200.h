@@ -91,7 +91,10 @@ NPU_B200_API int npu_b200_device_status(uint32_t* h_bits);
  *   d_workspace: npu_b200_flash_decode_workspace_size() bytes, zero-filled once
  *     before first use; the kernel returns it to zero-filled state itself, so
  *     calls on one stream may reuse it.  Calls that overlap on the GPU need
- *     separate workspaces. */
+ *     separate workspaces.
+ * The kernel is launched as a programmatic dependent of the stream's previous
+ * work: it reads no input and writes no output before that work has completed,
+ * so stream order is kept; only its launch overlaps that work's tail. */
 NPU_B200_API size_t npu_b200_flash_decode_workspace_size(int batch, int kv_heads, int head_dim, int max_seq,
                                             int num_splits);
 NPU_B200_API int npu_b200_flash_decode(const void* d_q, const void* d_k, const void* d_v,

@@ -876,7 +876,8 @@ size_t ring_bytes(int bn) {
 // Few tiles (fewer than one per CTA slot): split each tile's K over a cluster
 // and reduce through distributed shared memory -- no global scratch, no
 // serialized fix-up.  The cluster size is the largest for which every cluster
-// is resident at once: a second wave of clusters would double the time.
+// is resident at once, with slack: a second wave of clusters would double the
+// time.
 // Many tiles: stream-K over every CTA slot, where a tile has at most a couple
 // of contributors.
 Geometry geometry(int n_rows, int k, int batch) {
@@ -888,9 +889,13 @@ Geometry geometry(int n_rows, int k, int batch) {
   const long long slots_total = static_cast<long long>(sm_count()) * kCtasPerSm;
   g.split = 0;
   if (2ll * g.n_tiles <= slots_total) {
+    // Keep an eighth of the cluster slots free: with none spare, clusters
+    // placed while the previous kernel's CTAs still hold SMs fragment the
+    // GPCs, and the last clusters wait for a second wave (measured after the
+    // attention: o_proj's last 5% of CTAs started ~15 us after it ended).
     int best = 1;
     for (int s = 2; s <= kMaxCluster && g.kblocks / s >= 2; ++s)
-      if (g.n_tiles <= max_clusters(g.bn, s)) best = s;
+      if (8 * g.n_tiles <= 7 * max_clusters(g.bn, s)) best = s;
     g.split = best;
     g.grid = g.n_tiles * best;
     // Through L2 when the member's partial and its tokens of the others'

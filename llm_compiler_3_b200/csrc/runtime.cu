@@ -774,10 +774,16 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
     // 4 MB, ~5 us at 770 GB/s): at batch 64 over 8 ranks it saves 11 MB
     // (~14 us) per exchange; over 4 ranks 3 MB, where one hop less counts as
     // much.
+    // NPU_B200_TP_TWO_SHOT=1 / 0 forces it on (where the shape allows) / off;
+    // every rank must see the same setting.
     const int R = c->tp_size;
     const double saved = static_cast<double>(R - 1) * (R - 2) / R * batch * P.hidden * 8.0;
-    u.two_shot = R >= 3 && P.hidden % (32 * R) == 0 && saved > 4e6 &&
-                 static_cast<long long>(P.hidden / 128) * batch <= 16ll * sm_count();
+    const bool possible = P.hidden % (32 * R) == 0 &&
+                          static_cast<long long>(P.hidden / 128) * batch <= 16ll * sm_count();
+    const char* force = getenv("NPU_B200_TP_TWO_SHOT");
+    u.two_shot = possible && (force && force[0] == '1'   ? true
+                              : force && force[0] == '0' ? false
+                                                         : R >= 3 && saved > 4e6);
   }
   u.mode = kResidAddPartial;
   u.batch = batch;

@@ -74,8 +74,14 @@ __global__ void __launch_bounds__(kChunk)
       if (p.two_shot)
         px_put(p.px.part[p.px.rank] + px_reduced_offset(p.px, b, n), tag, __float_as_uint(sum));
     } else {
+      // The owner's warp publishes these 32 rows with one store instruction:
+      // one lane waits for the last word (one 8-byte poll per warp, not 32
+      // polls of NVLink while the owner is still adding), then all read.
+      const uint64_t* src = p.px.part[owner] + px_reduced_offset(p.px, b, n);
       uint32_t bits = 0;
-      px_get(p.px.part[owner] + px_reduced_offset(p.px, b, n), tag, &bits);
+      if (lane == 31) px_get(src, tag, &bits);
+      __syncwarp();
+      px_get(src, tag, &bits);
       sum = __uint_as_float(bits);
     }
     h = p.resid[static_cast<size_t>(b) * p.hidden + n] + sum;

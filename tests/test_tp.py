@@ -101,8 +101,10 @@ def _rank_main(rank, world, port, out_dir):
     top, layers, caches, tokens, hidden = _model(dev)
     kv_loc = s.kv_heads // world
     heads = slice(rank * kv_loc, (rank + 1) * kv_loc)
-    for exchange in ("peer", "nccl"):
-        os.environ["NPU_B200_TP_EXCHANGE"] = exchange
+    for exchange in ("peer", "peer2", "nccl"):
+        # peer2: the peer exchange with the two-shot all-reduce forced at batch 64
+        os.environ["NPU_B200_TP_EXCHANGE"] = "nccl" if exchange == "nccl" else "peer"
+        os.environ["NPU_B200_TP_TWO_SHOT"] = "1" if exchange == "peer2" else "0"
         box = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         with Decoder(plan, device=rank, tp_rank=rank, tp_size=world, nccl_id=box[0]) as dec:
@@ -206,11 +208,13 @@ def _close(got, want, what):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("batch", [1, 64])
-@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("exchange", ["peer", "peer2", "nccl"])
 def test_tensor_parallel_matches_oracle(world, batch, exchange):
     """Batch 1 runs the GEMV projections (the batch-1 all-reduce inside their
     residual epilogue), batch 64 the tensor-core ones with a separate residual
-    update; the all-reduces go over NVLink peer memory or through NCCL."""
+    update; the all-reduces go over NVLink peer memory (one-shot, or two-shot
+    with `peer2`: each rank adds its slice of rows and the others read the
+    sums) or through NCCL."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"tensor parallel over {world} ranks needs {world} GPUs")
     from test_decode import _check_ids
@@ -225,7 +229,7 @@ def test_tensor_parallel_matches_oracle(world, batch, exchange):
     ids = [load("ids", r) for r in range(world)]
     for r in range(world):
         peer, untouched, status = load("meta", r).tolist()
-        assert peer == (1 if exchange == "peer" else 0), f"rank {r}: exchange path {peer}"
+        assert peer == (0 if exchange == "nccl" else 1), f"rank {r}: exchange path {peer}"
         assert status == 0, f"rank {r}: device error bits {status}"
         assert untouched, f"rank {r}: a cache entry other than the new position changed"
         assert np.array_equal(ys[r], ys[0]), f"rank {r}: hidden states differ from rank 0"
