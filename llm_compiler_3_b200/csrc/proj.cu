@@ -270,21 +270,30 @@ __device__ __forceinline__ void run_epilogue_chunk(const EpiParams& ep, int tile
     }
     if (is_q || is_k) {  // RoPE: out_d = x_d cos - x_{d+64} sin, out_{d+64} = x_{d+64} cos + x_d sin
       const int i = r >> 1;
-      const float f = ep.inv_freq[i];
+      // The chunk's (cos, sin) first, as unconditional independent loads (tokens
+      // past the end read the last token's row): one memory round trip per
+      // chunk.  Loaded beside each token's shuffle, they cost one round trip
+      // per token (~10 us per batch-64 launch).
+      float2 cssn[kChunkCols];
+      if (ep.rope_tab != nullptr) {  // cos / sin of this step's positions, precomputed
+        const float2* tab = reinterpret_cast<const float2*>(ep.rope_tab) + i;
+#pragma unroll
+        for (int q = 0; q < kChunkCols; ++q) cssn[q] = __ldg(tab + min(b0 + q, batch - 1) * 64);
+      } else {
+        const float f = ep.inv_freq[i];
+#pragma unroll
+        for (int q = 0; q < kChunkCols; ++q) {
+          float sn, cs;
+          sincosf(static_cast<float>(pos_s[b0 + q]) * f, &sn, &cs);
+          cssn[q] = make_float2(cs, sn);
+        }
+      }
 #pragma unroll
       for (int q = 0; q < kChunkCols; ++q) {
         const float partner = __shfl_xor_sync(0xffffffffu, v[q], 1);
-        if (b0 + q < batch) {
-          float sn, cs;
-          if (ep.rope_tab != nullptr) {  // cos / sin of this step's positions, precomputed
-            const float2 cssn = reinterpret_cast<const float2*>(ep.rope_tab)[(b0 + q) * 64 + i];
-            cs = cssn.x;
-            sn = cssn.y;
-          } else {
-            sincosf(static_cast<float>(pos_s[b0 + q]) * f, &sn, &cs);
-          }
+        const float cs = cssn[q].x, sn = cssn[q].y;
+        if (b0 + q < batch)
           v[q] = (r & 1) == 0 ? v[q] * cs - partner * sn : v[q] * cs + partner * sn;
-        }
       }
     }
     if (is_q) {
