@@ -770,10 +770,11 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
     u.px = c->px;
     u.px.seq = seq;
     // Two-shot when the bytes it saves on each rank's NVLink, (R-1)(R-2)/R of
-    // the tagged partials, clearly outweigh its second hop and wait (taken as
-    // 4 MB, ~5 us at 770 GB/s): at batch 64 over 8 ranks it saves 11 MB
-    // (~14 us) per exchange; over 4 ranks 3 MB, where one hop less counts as
-    // much.
+    // the tagged partials, outweigh its second hop and wait: measured at two
+    // ranks, where both forms move the same bytes, 5.8 us per exchange more
+    // (batch 64: 6.67 against 6.29 ms per step), ~4.5 MB at 770 GB/s.  At
+    // batch 64 over 8 ranks it saves 11 MB (~14 us) per exchange; over 4
+    // ranks 3 MB, less than its cost.
     // NPU_B200_TP_TWO_SHOT=1 / 0 forces it on (where the shape allows) / off;
     // every rank must see the same setting.
     const int R = c->tp_size;
@@ -783,7 +784,7 @@ int residual_out(npu_b200_ctx* c, const __half* w, const void* x, int k, int bat
     const char* force = getenv("NPU_B200_TP_TWO_SHOT");
     u.two_shot = possible && (force && force[0] == '1'   ? true
                               : force && force[0] == '0' ? false
-                                                         : R >= 3 && saved > 4e6);
+                                                         : R >= 3 && saved > 4.5e6);
   }
   u.mode = kResidAddPartial;
   u.batch = batch;
