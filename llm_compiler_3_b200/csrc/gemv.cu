@@ -38,7 +38,7 @@ namespace {
 
 using namespace gemv;
 
-template <int BT>
+template <int BT, int KIND>
 __global__ void __launch_bounds__(kGemvThreads)
     gemv_kernel(const uint8_t* __restrict__ w_packed, const __half* __restrict__ x,
                 const __grid_constant__ EpiParams ep, int k, int kblocks, int n_groups,
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kGemvThreads)
     }
 #pragma unroll
     for (int b = 0; b < BT; ++b) acc[b] *= rn[b];
-    gemv_epilogue<BT>(ep, g, acc, pos_s, red, red_id);
+    gemv_epilogue<BT, KIND>(ep, g, acc, pos_s, red, red_id);
   }
 }
 
@@ -283,15 +283,15 @@ GemvLaunch choose_launch(int n_rows, int k) {
   return best;
 }
 
-template <int BT>
-int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams& ep,
-                cudaStream_t stream, bool pdl) {
+template <int BT, int KIND>
+int launch_gemv_kind(const void* w, const void* x, int n_rows, int k, const EpiParams& ep,
+                     cudaStream_t stream, bool pdl) {
   const GemvLaunch g = choose_launch<BT>(n_rows, k);
   NPU_REQUIRE(g.grid > 0, "gemv: activations of K=%d leave no room for the ring", k);
   const int kstages = (k / 64 + kPanelsPerStage - 1) / kPanelsPerStage;
   const int kx = g.split > 1 ? std::min(k, (kstages + g.split - 1) / g.split * kPanelsPerStage * 64) : k;
   const size_t smem = gemv_smem<BT>(kx, g.stages);
-  auto kern = gemv_kernel<BT>;
+  auto kern = gemv_kernel<BT, KIND>;
   // The limit is the function's, shared by the launches of every shape (and
   // by graph nodes a profiler relaunches after the capture): set it to the
   // most any launch may use, never to this launch's size.
@@ -309,6 +309,29 @@ int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams
   cfg.cluster = g.split;
   return launch(cfg, kern, static_cast<const uint8_t*>(w), static_cast<const __half*>(x), ep, k,
                 k / 64, n_rows / kRows, g.stages, g.split);
+}
+
+template <int BT>
+int launch_gemv(const void* w, const void* x, int n_rows, int k, const EpiParams& ep,
+                cudaStream_t stream, bool pdl) {
+  const bool peer = ep.px.seq >= 0;
+  switch (ep.kind) {
+    case kEpiStore:
+      return peer ? launch_gemv_kind<BT, kGemvStorePeer>(w, x, n_rows, k, ep, stream, pdl)
+                  : launch_gemv_kind<BT, kEpiStore>(w, x, n_rows, k, ep, stream, pdl);
+    case kEpiResid:
+      return peer ? launch_gemv_kind<BT, kGemvResidPeer>(w, x, n_rows, k, ep, stream, pdl)
+                  : launch_gemv_kind<BT, kEpiResid>(w, x, n_rows, k, ep, stream, pdl);
+    case kEpiSwiGLU:
+      return launch_gemv_kind<BT, kEpiSwiGLU>(w, x, n_rows, k, ep, stream, pdl);
+    case kEpiQKV:
+      return launch_gemv_kind<BT, kEpiQKV>(w, x, n_rows, k, ep, stream, pdl);
+    case kEpiArgmax:
+      return launch_gemv_kind<BT, kEpiArgmax>(w, x, n_rows, k, ep, stream, pdl);
+    default:
+      NPU_REQUIRE(false, "gemv: unknown epilogue kind %d", ep.kind);
+  }
+  return NPU_B200_E_INVALID;
 }
 
 }  // namespace

@@ -96,10 +96,17 @@ __device__ __forceinline__ void reduce_warps(const float (&c)[4][4], float* part
              part_sum[(3 * kRows + row) * 2 + b];
 }
 
+// Epilogue kinds of the kernel's instantiations: EpiParams::kind, plus the
+// STORE and RESID forms whose values go through the tensor-parallel exchange
+// (px.seq >= 0).  Each instantiation carries only its own epilogue: code that
+// is never taken still costs instruction fetch in a once-per-group path.
+constexpr int kGemvStorePeer = 16;
+constexpr int kGemvResidPeer = 17;
+
 // The fused epilogue of row group g: acc[b] is row (g * 16 + t / 8)'s FP32
 // value for token b (already RMSNorm-scaled), held by the 8 threads of the row;
 // every consumer thread calls this (it contains consumer barriers).
-template <int BT>
+template <int BT, int KIND>
 __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float (&acc)[BT],
                                               const int* pos_s, float* red, int* red_id) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -108,7 +115,7 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
   const int n = g * kRows + row;         // row of W
   const int tile = n >> 7, p = n & 127;  // 128-row tile and row within it
 
-  if (ep.kind == kEpiStore) {
+  if constexpr (KIND == kEpiStore || KIND == kGemvStorePeer) {
     if (lead) {
       const float bias = ep.bias ? __half2float(ep.bias[n]) : 0.f;
 #pragma unroll
@@ -117,7 +124,7 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
           float v = acc[b] + bias;
           if (ep.relu) v = fmaxf(v, 0.f);
           const size_t off = static_cast<size_t>(b) * ep.ld_out + n;
-          if (ep.px.seq >= 0)
+          if constexpr (KIND == kGemvStorePeer)
             px_store(ep.px, px_tag(ep.px, ep.px.seq), b, n, v);
           else if (ep.out_f32)
             static_cast<float*>(ep.out)[off] = v;
@@ -126,12 +133,12 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
         }
       }
     }
-  } else if (ep.kind == kEpiResid) {
+  } else if constexpr (KIND == kEpiResid || KIND == kGemvResidPeer) {
     // Tensor parallel: all-reduce first.  The lead thread stores this rank's
     // partial as a tagged word, reads every rank's word for (b, n) over
     // NVLink (px_gather: all missing ranks' loads in flight together, round
     // after round) and adds them in rank order, as every rank does.
-    if (ep.px.seq >= 0 && lead) {
+    if (KIND == kGemvResidPeer && lead) {
       const uint32_t tag = px_tag(ep.px, ep.px.seq);
 #pragma unroll
       for (int b = 0; b < BT; ++b)
@@ -168,7 +175,7 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
     if (t < BT && t < ep.batch)
       ep.ssq_out[static_cast<size_t>(g) * ep.ssq_out_ld + t] =
           red[t] + red[BT + t] + red[2 * BT + t] + red[3 * BT + t];
-  } else if (ep.kind == kEpiSwiGLU) {
+  } else if constexpr (KIND == kEpiSwiGLU) {
     // (gate_j, up_j) are rows (2j, 2j + 1).
 #pragma unroll
     for (int b = 0; b < BT; ++b) {
@@ -179,7 +186,7 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
             __float2half_rn(gt / (1.f + expf(-gt)) * up);
       }
     }
-  } else if (ep.kind == kEpiQKV) {
+  } else if constexpr (KIND == kEpiQKV) {
     // Head rows in pair order: row p holds dim (p >> 1) + 64 * (p & 1).
     const bool is_q = tile < ep.q_heads;
     const bool is_k = !is_q && tile < ep.q_heads + ep.kv_heads;
@@ -219,7 +226,7 @@ __device__ __forceinline__ void gemv_epilogue(const EpiParams& ep, int g, float 
         }
       }
     }
-  } else if (ep.kind == kEpiArgmax) {
+  } else if constexpr (KIND == kEpiArgmax) {
     // The group's (max, argmax) per token, lowest row on ties.
 #pragma unroll
     for (int b = 0; b < BT; ++b) {
