@@ -53,3 +53,23 @@ def test_flash_decode_workspace_sizes():
     size = lib.npu_b200_flash_decode_workspace_size(1, 8, 128, 4096, 16)
     assert size == 16384 * 4 + 8 * 16 * (8 * 128 + 16) * 4
     assert lib.npu_b200_flash_decode_workspace_size(1, 8, 128, 4096, 0) > 0
+
+
+@pytest.mark.parametrize("batch,kv_heads,keys,splits", [
+    (1, 1, 4096, 32),   # a TP=8 rank's single KV head: 32 CTAs of 128 keys
+    (1, 2, 4096, 32),
+    (1, 8, 4096, 16),   # config 2: 128 CTAs, one per SM
+    (16, 8, 8192, 8),   # config 4
+    (64, 8, 4096, 2),   # the batch-64 step: 1024 CTAs in ~7 waves
+    (1, 1, 300, 5),     # short cache: 64-key splits
+])
+def test_flash_decode_split_choice(batch, kv_heads, keys, splits):
+    """The automatic split count (waves of one CTA per SM on 148 SMs, ~96 keys of
+    start-up per CTA and ~6 keys of merge per split), read back from the
+    workspace it needs: counters + units x splits x (8 x head_dim + 16) floats."""
+    lib = _native.lib()
+    lib.npu_b200_flash_decode_workspace_size.restype = ctypes.c_size_t
+    size = lib.npu_b200_flash_decode_workspace_size(batch, kv_heads, 128, keys, 0)
+    per_split = batch * kv_heads * (8 * 128 + 16) * 4
+    assert (size - 16384 * 4) % per_split == 0
+    assert (size - 16384 * 4) // per_split == splits
